@@ -1,0 +1,376 @@
+#!/usr/bin/env python3
+"""Benchmark of the sm_100a FlashAttention-2 forward (the hot path) - driver contract.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload cfg2] [--scaling weak|strong]
+
+A step is one forward over one batch of synthetic seeded input (configuration 2
+by default: B8 H32 N4096 d128 bf16 causal, the configuration the headline target
+is quoted on), O and the logsumexp written.  Under torchrun each rank is one GPU;
+ranks process independent (batch x head) slices with no collective on the data
+path ("weak": every rank runs a full configuration-2 batch of its own slices;
+"strong": the configuration's slices are split across ranks).  Timing: W warm-up
+steps, then K steps between a barrier + synchronize on each side, device time from
+CUDA events on the launching stream, max over ranks.  Rank 0 prints one JSON line.
+
+`--impl reference` times the reference's own CPU attention
+(benchmark/cpp/correctness_v6.cu:23-72, built from its sources into oracle/_ref)
+on the host cores, one bounded sample of the same workload per step; it falls
+back to the restated oracle port if oracle/_ref was not built.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT, ROOT / "flash-attention_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+from flash_attention_runtime.inputs import CONFIGS, AttnConfig  # noqa: E402
+
+METRIC = "attention fwd TFLOPS/GPU (4*B*H*N^2*d/t, halved for causal)"
+REF_BUDGET_S = 150.0
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="cfg2", choices=sorted(CONFIGS))
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+# ----------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms in the background."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples = []  # (t, sm_mhz, max_mhz, reasons set)
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm, mx = float(parts[1]), float(parts[2])
+            except ValueError:
+                continue
+            names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+            reasons = {n for n, v in zip(names, parts[5:9]) if v.lower() == "active"}
+            self.samples.append((time.time(), sm, mx, reasons))
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+
+    def summary(self, t0: float, t1: float):
+        window = [s for s in self.samples if t0 <= s[0] <= t1]
+        use = window if window else self.samples
+        if not use:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        reasons = sorted(set().union(*[s[3] for s in use]))
+        return {"sm_mhz": statistics.median(s[1] for s in use), "sm_max_mhz": max(s[2] for s in use),
+                "reasons": reasons, "samples": len(use), "in_timed_window": bool(window)}
+
+
+# ----------------------------------------------------------------------------- CPU leg
+
+def cpu_sample(cfg: AttnConfig, n_slices: int, threads: int, use_ref: bool):
+    """Time the CPU attention on `n_slices` (b,h) slices of cfg; returns (seconds, kind)."""
+    from oracle import oracle as orc
+
+    g = torch.Generator(device="cpu")
+    g.manual_seed(cfg.seed)
+    shape = (1, n_slices, cfg.seq_len, cfg.head_dim)
+    q, k, v = (torch.randn(shape, generator=g).to(cfg.dtype).float().numpy() for _ in range(3))
+    t0 = time.perf_counter()
+    if use_ref:
+        orc.ref_attention(q, k, v, cfg.scale, cfg.causal, threads=threads)
+    else:
+        orc.oracle_attention(q, k, v, cfg.scale, cfg.causal, threads=threads)
+    return time.perf_counter() - t0
+
+
+def cpu_kind():
+    from oracle import oracle as orc
+
+    return orc.ref_available(), ("reference" if orc.ref_available() else "port")
+
+
+def run_reference_arm(args, cfg: AttnConfig):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return  # the reference CPU path does not shard; rank 0 alone runs it
+    from oracle import oracle as orc
+
+    use_ref, kind = cpu_kind()
+    threads = orc.host_threads()
+    n_slices = threads  # one slice per host thread per step
+    # A step takes seconds on the CPU: run at most one warm-up step, and only as
+    # many timed steps as fit in REF_BUDGET_S (the line reports the steps run).
+    warm = min(args.warmup, 1)
+    times = []
+    for _ in range(warm):
+        times.append(cpu_sample(cfg, n_slices, threads, use_ref))
+    est = times[0] if times else None
+    steps = args.steps if est is None else max(1, min(args.steps, int(REF_BUDGET_S / max(est, 1e-3))))
+    times = [cpu_sample(cfg, n_slices, threads, use_ref) for _ in range(steps)]
+    t = float(np.mean(times))
+    value = cfg.flops(n_slices) / t / 1e12
+    sample = (f"{n_slices} of {cfg.slices} (b,h) slices of {cfg.name} per step "
+              f"(N={cfg.seq_len}, d={cfg.head_dim}, causal={cfg.causal}), one per host thread")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world,
+        "steps": steps, "warmup": warm, "requested_steps": args.steps, "requested_warmup": args.warmup,
+        "ms_per_step": t * 1e3, "higher_is_better": True,
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(cfg, world, args.scaling),
+        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": threads, "kind": kind, "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU leg
+
+def workload_config(cfg: AttnConfig, world: int, scaling: str):
+    per_rank_b = cfg.batch if scaling == "weak" else cfg.batch  # slices split below for strong
+    return {
+        "workload": cfg.name, "batch_per_rank": per_rank_b if scaling == "weak" else None,
+        "global_batch": cfg.batch * world if scaling == "weak" else cfg.batch,
+        "heads": cfg.heads, "seq_len": cfg.seq_len, "head_dim": cfg.head_dim, "causal": cfg.causal,
+        "input_dtype": str(cfg.dtype).replace("torch.", ""), "parallelism": f"bh-shard x{world}",
+        "l2": "inputs larger than L2 (Q+K+V per rank >> 126 MB); no flush needed",
+        "lse": True,
+    }
+
+
+def rank_inputs(cfg: AttnConfig, rank: int, world: int, scaling: str, dev):
+    """This rank's Q, K, V on `dev` (drawn on the CPU, seeded per rank)."""
+    from flash_attention_runtime.inputs import generate
+
+    if scaling == "weak":
+        q, k, v = generate(cfg, seed_offset=1000 * rank)
+        n_slices = cfg.slices
+    else:
+        q, k, v = generate(cfg)
+        s = cfg.slices
+        lo, hi = rank * s // world, (rank + 1) * s // world
+        flat = lambda t: t.reshape(s, cfg.seq_len, cfg.head_dim)[lo:hi]  # noqa: E731
+        q, k, v = (flat(t).reshape(1, hi - lo, cfg.seq_len, cfg.head_dim).contiguous() for t in (q, k, v))
+        n_slices = hi - lo
+    return q, k, v, n_slices
+
+
+def run_ours(args, cfg: AttnConfig):
+    import torch.distributed as dist
+
+    import flash_attention_runtime as fa
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    qh, kh, vh, n_slices = rank_inputs(cfg, rank, world, args.scaling, dev)
+    q, k, v = qh.to(dev), kh.to(dev), vh.to(dev)
+    o = torch.empty_like(q)
+    lse = torch.empty(q.shape[:3], dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        fa.ext_forward(q, k, v, o, False, cfg.scale, cfg.causal, lse)
+
+    fa.reset_device_status(dev)
+    sampler = ClockSampler(local)
+    sampler.start()
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    t_wall0 = time.time()
+    for i in range(args.steps):
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    torch.cuda.synchronize(dev)
+    t_wall1 = time.time()
+    barrier()
+    total_ms = starts[0].elapsed_time(ends[-1])
+    launch_ms = float(np.mean([s.elapsed_time(e) for s, e in zip(starts, ends)]))
+    sampler.stop()
+    status = fa.device_status(dev)
+    if status != 0:
+        raise RuntimeError(f"kernel status 0x{status:x}")
+
+    ms_per_step = max_over_ranks(total_ms / args.steps)
+    launch_ms_max = max_over_ranks(launch_ms)
+    flops_rank = cfg.flops(n_slices)
+    total_flops = flops_rank * world if args.scaling == "weak" else cfg.flops()
+    value = total_flops / (ms_per_step * 1e-3) / 1e12
+
+    # ---- end to end through the public API: pinned host -> device, forward, device -> host
+    e2e_steps = args.e2e_steps if args.e2e_steps is not None else max(3, min(20, args.steps // 50))
+    e2e_steps = max(1, e2e_steps)
+    qp, kp, vp = (t.pin_memory() for t in (qh, kh, vh))
+    op = torch.empty(qh.shape, dtype=qh.dtype).pin_memory()
+    lp = torch.empty(qh.shape[:3], dtype=torch.float32).pin_memory()
+    qd, kd, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+    def e2e_step():
+        qd.copy_(qp, non_blocking=True)
+        kd.copy_(kp, non_blocking=True)
+        vd.copy_(vp, non_blocking=True)
+        fa.ext_forward(qd, kd, vd, o, False, cfg.scale, cfg.causal, lse)
+        op.copy_(o, non_blocking=True)
+        lp.copy_(lse, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+    e2e_value = total_flops / (e2e_ms * 1e-3) / 1e12
+    h2d = sum(t.numel() * t.element_size() for t in (qh, kh, vh))
+    d2h = op.numel() * op.element_size() + lp.numel() * lp.element_size()
+
+    peaks, peak_src = load_peaks()
+    peak = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    achieved = flops_rank / (launch_ms_max * 1e-3) / 1e12
+    traffic = None
+    tfile = ROOT / "profiles" / f"traffic_{cfg.name}.json"
+    if tfile.exists():
+        try:
+            traffic = json.loads(tfile.read_text()).get("bytes_per_launch")
+        except (ValueError, OSError):
+            traffic = None
+
+    result = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            from oracle import oracle as orc
+
+            use_ref, kind = cpu_kind()
+            threads = orc.host_threads()
+            n_cpu = max(1, threads)
+            secs = cpu_sample(cfg, n_cpu, threads, use_ref)
+            cpu = {"value": cfg.flops(n_cpu) / secs / 1e12, "unit": "TFLOPS", "cores": threads, "kind": kind,
+                   "sample": f"{n_cpu} (b,h) slices of {cfg.name} (N={cfg.seq_len}, d={cfg.head_dim}, "
+                             f"causal={cfg.causal}), one per host thread, {secs:.1f} s"}
+        result = {
+            "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": args.scaling, "vs_baseline": None, "dtype": "bf16" if cfg.dtype == torch.bfloat16 else "f16",
+            "data": "synthetic (seeded N(0,1), generated on CPU)",
+            "config": workload_config(cfg, world, args.scaling),
+            "e2e": {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_ms, "steps": e2e_steps},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": f"{peak_src} bf16_tflops_sustained (kernel timed back to back)",
+                         "frac_of_burst_peak": achieved / float(peaks.get("bf16_tflops", peak)),
+                         "kernel": "fa_fwd_sm100_kernel", "launch_ms": launch_ms_max,
+                         "algorithmic_flops_per_launch": flops_rank},
+            "cpu_baseline": cpu,
+            "clocks": sampler.summary(t_wall0, t_wall1),
+            "gpu_launches": args.steps,
+        }
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return result
+
+
+def main():
+    args = parse_args()
+    cfg = CONFIGS[args.workload]
+    if args.impl == "reference":
+        run_reference_arm(args, cfg)
+        return
+    run_ours(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,499 @@
+// Warp-specialised FlashAttention-2 forward for sm_100a (B200).
+//
+// Replaces the reference's live kernel flash_attention_forward_v6_mma
+// (src/forward/forward_v6_mma.cuh:325-412), which computes one 64-row query tile
+// per CTA with sm_80 mma.sync.  Same mathematics (softmax(scale*Q K^T [+causal]) V
+// with the online softmax of src/softmax/online_softmax.cuh:13-252), new machine:
+//
+//  * one persistent CTA per SM; a CTA work unit ("tile") is a pair of 128-row
+//    query tiles Q0, Q1 of one (batch, head) slice, handed out by an atomic
+//    counter in a global workspace (LPT order for causal, grouped by slice so the
+//    K/V of the slices in flight stay in L2);
+//  * warp 8  : TMA producer  - Q0/Q1 once per tile, K_j / V_j through a ring of
+//              STAGES shared-memory stages (mbarrier full/empty pairs);
+//  * warp 9  : MMA issuer    - tcgen05.mma S_i = Q_i K_j^T (smem x smem -> TMEM)
+//              and O_i += P_i V_j (P from TMEM, V from smem, O in TMEM);
+//  * warps 0-3 / 4-7 : softmax warpgroup i for query tile i, one thread per row
+//              (= TMEM lane): tcgen05.ld of the S row, mask, row max, exp2 with the
+//              scale folded in, row sum, P rounded to the input type and written
+//              back into the S columns with tcgen05.st; lazy O rescale (only when
+//              the running max grows by more than 2^8); final 1/l normalise, O
+//              store and logsumexp.
+//
+// TMEM (512 columns x 128 lanes of 32 bit): S0 [0,128) S1 [128,256)
+// O0 [256,256+D) O1 [256+D,256+2D); P_i aliases the first 64 columns of S_i.
+//
+// Every mbarrier wait is bounded in time: on expiry the CTA records a status
+// code, raises a shared abort flag that ends every other role's waits, drains its
+// own copies and MMAs in flight, frees TMEM and returns.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#include "ptx.cuh"
+#include "umma_layout.h"
+
+namespace fa {
+
+struct KernelParams {
+  void* O;
+  float* LSE;
+  int64_t o_stride_b, o_stride_h, o_stride_s;  // elements
+  int batch, heads, seq_len;
+  float scale_log2;  // softmax_scale * log2(e)
+  int n_pairs;       // ceil(N / 256): query-tile pairs per slice
+  int n_kv;          // ceil(N / 128): key/value blocks per slice
+  int num_tiles;     // batch * heads * n_pairs
+  int group_bh;      // slices per scheduling group
+  int* tile_counter; // workspace word, zero at launch
+  int* status;       // optional device status word (may be null)
+  unsigned long long timeout_ns;
+};
+
+// Status codes written to KernelParams::status: 0x100 | where.
+enum : int {
+  kWaitSched = 1, kWaitQEmpty, kWaitKvEmpty, kWaitQFull, kWaitKvFull, kWaitPFull, kWaitOEmpty,
+  kWaitSFull, kWaitOFull,
+};
+
+constexpr int kBlockM = 128;
+constexpr int kBlockN = 128;
+constexpr int kNumThreads = 320;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only if the max grew by > 2^8
+
+template <int D>
+struct Cfg {
+  static constexpr uint32_t SW = swizzle_bytes(D);
+  static constexpr int CHUNKS = D * 2 / SW;
+  static constexpr uint32_t TILE_BYTES = kBlockM * D * 2;  // Q, K and V tiles are all 128 x D
+  static constexpr int STAGES = D == 128 ? 4 : (D == 64 ? 6 : 8);
+  static constexpr uint32_t Q_OFF = 0;
+  static constexpr uint32_t KV_OFF = 2 * TILE_BYTES;
+  static constexpr uint32_t BAR_OFF = KV_OFF + STAGES * TILE_BYTES;
+  // barriers: sched_full[2] sched_empty[2] q_full[2] q_empty[2] s_full[2] p_full[2]
+  //           o_full[2] o_empty[2] drain[1] kv_full[S] kv_empty[S]
+  static constexpr int NBARS = 17 + 2 * STAGES;
+  static constexpr uint32_t MISC_OFF = BAR_OFF + NBARS * 8;  // tmem slot, sched slots, abort flag
+  static constexpr uint32_t SMEM_BYTES = MISC_OFF + 64 + 1024;  // + alignment slack
+  static constexpr uint32_t TMEM_COLS = 512;
+  // TMEM columns of S_i (P_i aliases its first 64 columns) and of O_i.
+  __host__ __device__ static constexpr uint32_t s_col(int i) { return 128u * i; }
+  __host__ __device__ static constexpr uint32_t o_col(int i) { return 256u + D * i; }
+};
+
+__device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                             const KernelParams& p, int where) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 31u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > p.timeout_ns) {
+        *abort_flag = 1;
+        if (p.status) atomicCAS(p.status, 0, 0x100 | where);
+        return false;
+      }
+    }
+  }
+}
+
+// Wait that ignores the abort flag; used only to drain work already in flight.
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > limit_ns) return;
+  }
+}
+
+struct TileInfo {
+  int b, h, pair, n0, n1;
+};
+
+template <bool CAUSAL>
+__device__ __forceinline__ TileInfo decode_tile(int tile, const KernelParams& p) {
+  const int bh_total = p.batch * p.heads;
+  const int per_group = p.group_bh * p.n_pairs;
+  const int g = tile / per_group;
+  const int r = tile - g * per_group;
+  const int gsize = min(p.group_bh, bh_total - g * p.group_bh);
+  const int rank = r / gsize;
+  const int bh = g * p.group_bh + (r - rank * gsize);
+  TileInfo t;
+  t.b = bh / p.heads;
+  t.h = bh - t.b * p.heads;
+  t.pair = CAUSAL ? (p.n_pairs - 1 - rank) : rank;
+  const int q0 = t.pair * 256;
+  const int q1 = q0 + 128;
+  t.n0 = CAUSAL ? min(2 * t.pair + 1, p.n_kv) : p.n_kv;
+  t.n1 = q1 >= p.seq_len ? 0 : (CAUSAL ? min(2 * t.pair + 2, p.n_kv) : p.n_kv);
+  return t;
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (BF16) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
+template <int D, bool BF16, bool CAUSAL>
+__global__ void __launch_bounds__(kNumThreads, 1)
+    fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV, const KernelParams p) {
+  using C = Cfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + C::BAR_OFF;
+  auto bar = [&](int i) -> uint32_t { return bar0 + 8u * i; };
+  // barrier indices
+  const uint32_t SCHED_FULL = 0, SCHED_EMPTY = 2, Q_FULL = 4, Q_EMPTY = 6, S_FULL = 8, P_FULL = 10,
+                 O_FULL = 12, O_EMPTY = 14, DRAIN = 16, KV_FULL = 17, KV_EMPTY = 17 + C::STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::MISC_OFF);
+  volatile int* sched_tile = reinterpret_cast<volatile int*>(smem + C::MISC_OFF + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::MISC_OFF + 32);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(SCHED_FULL + i), 1);
+      mbar_init(bar(SCHED_EMPTY + i), 1 + 256);
+      mbar_init(bar(Q_FULL + i), 1);
+      mbar_init(bar(Q_EMPTY + i), 1);
+      mbar_init(bar(S_FULL + i), 1);
+      mbar_init(bar(P_FULL + i), 128);
+      mbar_init(bar(O_FULL + i), 1);
+      mbar_init(bar(O_EMPTY + i), 128);
+    }
+    mbar_init(bar(DRAIN), 1);
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(bar(KV_FULL + s), 1);
+      mbar_init(bar(KV_EMPTY + s), 1);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  if (warp == kProducerWarp && lane == 0) {
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+
+  if (warp == kProducerWarp) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint64_t pol_kv = l2_policy_evict_last();
+      const uint64_t pol_q = l2_policy_evict_first();
+      int tile = blockIdx.x;
+      uint32_t sched_cnt = 0, kv_cnt = 0, q_cnt[2] = {0, 0};
+      // phase parity of the last arming of each full barrier, for the abort drain
+      uint32_t kv_armed = 0, q_armed = 0;  // bit s: armed and maybe in flight
+      uint32_t kv_par = 0, q_par = 0;      // bit s: parity armed
+      bool ok = true;
+      auto load_q = [&](int i, const TileInfo& t) -> bool {
+        if (!bounded_wait(bar(Q_EMPTY + i), (q_cnt[i] & 1) ^ 1, abort_flag, p, kWaitQEmpty)) return false;
+        const uint32_t fb = bar(Q_FULL + i);
+        mbar_arrive_expect_tx(fb, C::TILE_BYTES);
+        q_armed |= 1u << i;
+        q_par = (q_par & ~(1u << i)) | ((q_cnt[i] & 1) << i);
+        const uint32_t dst = sbase + C::Q_OFF + i * C::TILE_BYTES;
+#pragma unroll
+        for (int c = 0; c < C::CHUNKS; ++c)
+          tma_load_4d(dst + c * kBlockM * C::SW, &tmQ, fb, c * int(C::SW / 2), t.pair * 256 + i * 128, t.h, t.b,
+                      pol_q);
+        ++q_cnt[i];
+        return true;
+      };
+      auto load_kv = [&](const CUtensorMap* m, int j, const TileInfo& t) -> bool {
+        const uint32_t s = kv_cnt % C::STAGES;
+        const uint32_t ph = (kv_cnt / C::STAGES) & 1;
+        if (!bounded_wait(bar(KV_EMPTY + s), ph ^ 1, abort_flag, p, kWaitKvEmpty)) return false;
+        const uint32_t fb = bar(KV_FULL + s);
+        mbar_arrive_expect_tx(fb, C::TILE_BYTES);
+        kv_armed |= 1u << s;
+        kv_par = (kv_par & ~(1u << s)) | (ph << s);
+        const uint32_t dst = sbase + C::KV_OFF + s * C::TILE_BYTES;
+#pragma unroll
+        for (int c = 0; c < C::CHUNKS; ++c)
+          tma_load_4d(dst + c * kBlockN * C::SW, m, fb, c * int(C::SW / 2), j * kBlockN, t.h, t.b, pol_kv);
+        ++kv_cnt;
+        return true;
+      };
+      while (ok) {
+        const uint32_t slot = sched_cnt & 1;
+        if (!bounded_wait(bar(SCHED_EMPTY + slot), ((sched_cnt >> 1) & 1) ^ 1, abort_flag, p, kWaitSched)) break;
+        sched_tile[slot] = tile;
+        mbar_arrive(bar(SCHED_FULL + slot));
+        ++sched_cnt;
+        if (tile >= p.num_tiles) break;
+        const int next = atomicAdd(p.tile_counter, 1) + static_cast<int>(gridDim.x);
+        const TileInfo t = decode_tile<CAUSAL>(tile, p);
+        const int nmax = max(t.n0, t.n1);
+        ok = load_q(0, t) && load_kv(&tmK, 0, t);
+        if (ok && t.n1 > 0) ok = load_q(1, t);
+        for (int j = 0; ok && j < nmax; ++j) {
+          ok = load_kv(&tmV, j, t);
+          if (ok && j + 1 < nmax) ok = load_kv(&tmK, j + 1, t);
+        }
+        tile = next;
+      }
+      if (*abort_flag) {
+        // Let every copy this thread started land before the CTA exits.
+        for (int s = 0; s < C::STAGES; ++s)
+          if (kv_armed & (1u << s)) drain_wait(bar(KV_FULL + s), (kv_par >> s) & 1, 200000000ull);
+        for (int i = 0; i < 2; ++i)
+          if (q_armed & (1u << i)) drain_wait(bar(Q_FULL + i), (q_par >> i) & 1, 200000000ull);
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = make_idesc_f16(BF16, kBlockM, kBlockN, false, false);
+      constexpr uint32_t idesc_pv = make_idesc_f16(BF16, kBlockM, D, false, true);
+      uint32_t sched_cnt = 0, kv_cnt = 0, qf_cnt[2] = {0, 0}, pf_cnt[2] = {0, 0}, oe_cnt[2] = {0, 0};
+      bool ok = true;
+      auto acquire = [&](uint32_t& stage) -> bool {
+        stage = kv_cnt % C::STAGES;
+        const uint32_t ph = (kv_cnt / C::STAGES) & 1;
+        ++kv_cnt;
+        return bounded_wait(bar(KV_FULL + stage), ph, abort_flag, p, kWaitKvFull);
+      };
+      auto issue_s = [&](int i, uint32_t stage) {
+        const uint32_t qb = sbase + C::Q_OFF + i * C::TILE_BYTES;
+        const uint32_t kb = sbase + C::KV_OFF + stage * C::TILE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma_ss(tmem_base + C::s_col(i), kmajor_desc(qb, kBlockM, C::SW, kk), kmajor_desc(kb, kBlockN, C::SW, kk),
+                  idesc_qk, kk > 0 ? 1u : 0u);
+      };
+      auto issue_pv = [&](int i, uint32_t stage, bool accumulate) {
+        const uint32_t vb = sbase + C::KV_OFF + stage * C::TILE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < kBlockN / 16; ++kk)
+          umma_ts(tmem_base + C::o_col(i), tmem_base + C::s_col(i) + kk * 8, mnmajor_desc(vb, kBlockN, C::SW, kk),
+                  idesc_pv, (accumulate || kk > 0) ? 1u : 0u);
+      };
+      auto wait_p = [&](int i, int j) -> bool {
+        if (!bounded_wait(bar(P_FULL + i), pf_cnt[i] & 1, abort_flag, p, kWaitPFull)) return false;
+        ++pf_cnt[i];
+        if (j == 0) {
+          if (!bounded_wait(bar(O_EMPTY + i), (oe_cnt[i] & 1) ^ 1, abort_flag, p, kWaitOEmpty)) return false;
+          ++oe_cnt[i];
+        }
+        tc_fence_after();
+        return true;
+      };
+      while (ok) {
+        const uint32_t slot = sched_cnt & 1;
+        if (!bounded_wait(bar(SCHED_FULL + slot), (sched_cnt >> 1) & 1, abort_flag, p, kWaitSched)) break;
+        const int tile = sched_tile[slot];
+        mbar_arrive(bar(SCHED_EMPTY + slot));
+        ++sched_cnt;
+        if (tile >= p.num_tiles) break;
+        const TileInfo t = decode_tile<CAUSAL>(tile, p);
+        const int n0 = t.n0, n1 = t.n1, nmax = max(n0, n1);
+        uint32_t sk;
+        ok = acquire(sk) && bounded_wait(bar(Q_FULL + 0), qf_cnt[0] & 1, abort_flag, p, kWaitQFull);
+        if (!ok) break;
+        ++qf_cnt[0];
+        tc_fence_after();
+        issue_s(0, sk);
+        umma_commit(bar(S_FULL + 0));
+        if (n0 == 1) umma_commit(bar(Q_EMPTY + 0));
+        if (n1 > 0) {
+          if (!bounded_wait(bar(Q_FULL + 1), qf_cnt[1] & 1, abort_flag, p, kWaitQFull)) break;
+          ++qf_cnt[1];
+          tc_fence_after();
+          issue_s(1, sk);
+          umma_commit(bar(S_FULL + 1));
+          if (n1 == 1) umma_commit(bar(Q_EMPTY + 1));
+        }
+        umma_commit(bar(KV_EMPTY + sk));
+        for (int j = 0; j < nmax; ++j) {
+          uint32_t sv, skn = 0;
+          if (!acquire(sv)) { ok = false; break; }
+          tc_fence_after();
+          const bool has_next = j + 1 < nmax;
+          if (j < n0) {
+            if (!wait_p(0, j)) { ok = false; break; }
+            issue_pv(0, sv, j > 0);
+            if (j == n0 - 1) umma_commit(bar(O_FULL + 0));
+          }
+          if (has_next) {
+            if (!acquire(skn)) { ok = false; break; }
+            tc_fence_after();
+          }
+          if (j + 1 < n0) {
+            issue_s(0, skn);
+            umma_commit(bar(S_FULL + 0));
+            if (j + 2 == n0) umma_commit(bar(Q_EMPTY + 0));
+          }
+          if (j < n1) {
+            if (!wait_p(1, j)) { ok = false; break; }
+            issue_pv(1, sv, j > 0);
+            if (j == n1 - 1) umma_commit(bar(O_FULL + 1));
+          }
+          if (j + 1 < n1) {
+            issue_s(1, skn);
+            umma_commit(bar(S_FULL + 1));
+            if (j + 2 == n1) umma_commit(bar(Q_EMPTY + 1));
+          }
+          umma_commit(bar(KV_EMPTY + sv));
+          if (has_next) umma_commit(bar(KV_EMPTY + skn));
+        }
+      }
+      // Every MMA issued by this thread completes before TMEM and smem go away.
+      umma_commit(bar(DRAIN));
+      drain_wait(bar(DRAIN), 0, 200000000ull);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax warpgroups
+    const int wg = warp / 4;                      // query tile 0 or 1
+    const int row_in_tile = threadIdx.x % 128;    // = TMEM lane
+    const uint32_t lane_addr = static_cast<uint32_t>((warp % 4) * 32) << 16;
+    const uint32_t s_addr = tmem_base + lane_addr + C::s_col(wg);
+    const uint32_t o_addr = tmem_base + lane_addr + C::o_col(wg);
+    uint32_t sched_cnt = 0, s_cnt = 0, o_cnt = 0;
+    const float sl2 = p.scale_log2;
+    while (true) {
+      const uint32_t slot = sched_cnt & 1;
+      bool ok = bounded_wait(bar(SCHED_FULL + slot), (sched_cnt >> 1) & 1, abort_flag, p, kWaitSched);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      const int tile = sched_tile[slot];
+      mbar_arrive(bar(SCHED_EMPTY + slot));
+      ++sched_cnt;
+      if (tile >= p.num_tiles) break;
+      const TileInfo t = decode_tile<CAUSAL>(tile, p);
+      const int n = wg == 0 ? t.n0 : t.n1;
+      if (n == 0) continue;
+      const int row = t.pair * 256 + wg * 128 + row_in_tile;
+      float m_ref = -INFINITY, l = 0.f;
+      bool failed = false;
+      for (int j = 0; j < n; ++j) {
+        ok = bounded_wait(bar(S_FULL + wg), s_cnt & 1, abort_flag, p, kWaitSFull);
+        if (!__all_sync(0xffffffffu, ok)) { failed = true; break; }
+        ++s_cnt;
+        tc_fence_after();
+        float s[kBlockN];
+#pragma unroll
+        for (int c = 0; c < kBlockN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(s_addr + c * 32, r);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(r[e]);
+        }
+        tmem_wait_ld();
+        if (j == n - 1 && (CAUSAL || (p.seq_len % kBlockN) != 0)) {
+          const int k0 = j * kBlockN;
+          int lim = p.seq_len - 1 - k0;
+          if (CAUSAL) lim = min(lim, row - k0);
+#pragma unroll
+          for (int c = 0; c < kBlockN; ++c) s[c] = c > lim ? -INFINITY : s[c];
+        }
+        float mt = s[0];
+#pragma unroll
+        for (int c = 1; c < kBlockN; ++c) mt = fmaxf(mt, s[c]);
+        const float m_new = fmaxf(m_ref, mt);
+        if (j == 0) {
+          m_ref = m_new;
+        } else {
+          const bool need = (m_new - m_ref) * sl2 > kRescaleThreshold;
+          if (__any_sync(0xffffffffu, need)) {
+            const float alpha = need ? ex2_approx((m_ref - m_new) * sl2) : 1.f;
+            if (need) {
+              l *= alpha;
+              m_ref = m_new;
+            }
+#pragma unroll 1
+            for (int c = 0; c < D / 32; ++c) {
+              uint32_t r[32];
+              tmem_ld32(o_addr + c * 32, r);
+              tmem_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+              tmem_st32(o_addr + c * 32, r);
+            }
+          }
+        }
+        const float mc = m_ref == -INFINITY ? 0.f : m_ref * sl2;
+        float lsum = 0.f;
+#pragma unroll
+        for (int c = 0; c < kBlockN / 64; ++c) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float p0 = ex2_approx(fmaf(s[c * 64 + 2 * e], sl2, -mc));
+            const float p1 = ex2_approx(fmaf(s[c * 64 + 2 * e + 1], sl2, -mc));
+            lsum += p0 + p1;
+            pk[e] = pack2<BF16>(p0, p1);
+          }
+          tmem_st32(s_addr + c * 32, pk);
+        }
+        l += lsum;
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar(P_FULL + wg));
+      }
+      if (failed) break;
+      ok = bounded_wait(bar(O_FULL + wg), o_cnt & 1, abort_flag, p, kWaitOFull);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      ++o_cnt;
+      tc_fence_after();
+      const float inv_l = 1.f / l;
+      const bool row_ok = row < p.seq_len;
+      uint8_t* orow = reinterpret_cast<uint8_t*>(p.O) +
+                      2 * (t.b * p.o_stride_b + t.h * p.o_stride_h + static_cast<int64_t>(row) * p.o_stride_s);
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        __syncwarp();
+        uint32_t r[32];
+        tmem_ld32(o_addr + c * 32, r);
+        tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          pk[e] = pack2<BF16>(__uint_as_float(r[2 * e]) * inv_l, __uint_as_float(r[2 * e + 1]) * inv_l);
+        if (row_ok) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) st_global_v4(orow + c * 64 + v * 16, pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+        }
+      }
+      if (row_ok && p.LSE != nullptr) {
+        const float lse2 = (m_ref == -INFINITY ? 0.f : m_ref * sl2) + log2f(l);
+        p.LSE[(static_cast<int64_t>(t.b) * p.heads + t.h) * p.seq_len + row] = lse2 * 0.69314718055994531f;
+      }
+      tc_fence_before();
+      mbar_arrive(bar(O_EMPTY + wg));
+    }
+    tc_fence_before();
+  }
+
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+}  // namespace fa

@@ -1,0 +1,63 @@
+// Internal interface between the C-ABI front end (fa_sm100.cu) and the per-head-dim
+// translation units that instantiate the kernel (fa_fwd_d{32,64,128}.cu).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "fa_fwd_kernel.cuh"
+
+namespace fa {
+
+struct LaunchSpec {
+  CUtensorMap tq, tk, tv;
+  KernelParams kp;
+  int grid;
+  cudaStream_t stream;
+  bool bf16;
+  bool causal;
+};
+
+cudaError_t launch_d32(const LaunchSpec& s);
+cudaError_t launch_d64(const LaunchSpec& s);
+cudaError_t launch_d128(const LaunchSpec& s);
+
+// Sets the dynamic-smem attribute of one kernel instantiation once per device.
+template <typename Kernel>
+cudaError_t ensure_smem_attr(Kernel k, int smem_bytes, unsigned* done_mask) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned bit = 1u << (dev & 31);
+  if (__atomic_load_n(done_mask, __ATOMIC_ACQUIRE) & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+  if (e != cudaSuccess) return e;
+  __atomic_fetch_or(done_mask, bit, __ATOMIC_ACQ_REL);
+  return cudaSuccess;
+}
+
+template <int D>
+cudaError_t launch_for_dim(const LaunchSpec& s) {
+  constexpr int smem = static_cast<int>(Cfg<D>::SMEM_BYTES);
+  static unsigned done[4] = {0, 0, 0, 0};
+  const int v = (s.bf16 ? 1 : 0) | (s.causal ? 2 : 0);
+  cudaError_t e;
+  switch (v) {
+#define FA_CASE(IDX, BF, CA)                                                       \
+  case IDX:                                                                        \
+    e = ensure_smem_attr(fa_fwd_sm100_kernel<D, BF, CA>, smem, &done[IDX]);       \
+    if (e != cudaSuccess) return e;                                                \
+    fa_fwd_sm100_kernel<D, BF, CA><<<s.grid, kNumThreads, smem, s.stream>>>(s.tq, s.tk, s.tv, s.kp); \
+    break;
+    FA_CASE(0, false, false)
+    FA_CASE(1, true, false)
+    FA_CASE(2, false, true)
+    FA_CASE(3, true, true)
+#undef FA_CASE
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace fa

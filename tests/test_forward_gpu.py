@@ -1,0 +1,175 @@
+"""GPU parity tests: the sm_100a kernel (through the C ABI, via flash_attention_runtime)
+against the CPU oracle restating the reference's cpu_reference_attention
+(benchmark/cpp/correctness_v6.cu:23-72) on the same seeded, dtype-rounded inputs.
+
+Sizes are ones the oracle finishes in seconds; full-size configurations are
+checked through size-independent properties at the end of this file.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.oracle import oracle_attention
+from parity import compare_lse, compare_output
+
+import flash_attention_runtime as fa
+from flash_attention_runtime.inputs import CONFIGS, generate, make_random, make_stress, make_structured
+
+pytestmark = pytest.mark.gpu
+
+
+def _run_and_check(q, k, v, causal, scale=None, slices=None, atol=None, rtol=0.0):
+    dev = torch.device("cuda", 0)
+    dtype = q.dtype
+    d = q.shape[-1]
+    scale = 1.0 / math.sqrt(d) if scale is None else scale
+    qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
+    fa.reset_device_status(dev)
+    out, lse = fa.forward(qd, kd, vd, softmax_scale=scale, causal=causal, return_lse=True)
+    torch.cuda.synchronize(dev)
+    assert fa.device_status(dev) == 0
+    ref_o, ref_lse = oracle_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), scale, causal,
+                                      slices=slices)
+    if slices is not None:
+        b, h = q.shape[:2]
+        s0, s1 = slices
+        out = out.reshape(b * h, *out.shape[2:])[s0:s1]
+        lse = lse.reshape(b * h, -1)[s0:s1]
+        ref_o = ref_o.reshape(b * h, *ref_o.shape[2:])[s0:s1]
+        ref_lse = ref_lse.reshape(b * h, -1)[s0:s1]
+    ro = compare_output(out, ref_o, dtype, atol=atol, rtol=rtol)
+    rl = compare_lse(lse, ref_lse)
+    assert ro["ok"], ro
+    assert rl["ok"], rl
+    return ro, rl
+
+
+def test_cfg0_correctness_case():
+    """Config 0: B1 H4 N256 d64 fp16, seed 0, non-causal, scale 1/8, with LSE."""
+    cfg = CONFIGS["cfg0"]
+    q, k, v = generate(cfg)
+    _run_and_check(q, k, v, cfg.causal, cfg.scale)
+
+
+def test_cfg1_full():
+    """Config 1: B4 H16 N1024 d64 fp16, seed 1, non-causal - every slice checked."""
+    cfg = CONFIGS["cfg1"]
+    q, k, v = generate(cfg)
+    _run_and_check(q, k, v, cfg.causal, cfg.scale)
+
+
+@pytest.mark.parametrize("d", [32, 64, 128])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("causal", [False, True])
+def test_head_dims_dtypes_masks(d, dtype, causal):
+    q, k, v = make_random((2, 3, 512, d), dtype, seed=100 + d)
+    _run_and_check(q, k, v, causal)
+
+
+@pytest.mark.parametrize("n", [1, 7, 64, 127, 128, 129, 200, 255, 256, 257, 383, 640, 1000])
+@pytest.mark.parametrize("causal", [False, True])
+def test_ragged_seq_len(n, causal):
+    """Sequence lengths that are not multiples of the 128-row tiles (tail masking)."""
+    q, k, v = make_random((1, 2, n, 64), torch.bfloat16, seed=7 + n)
+    _run_and_check(q, k, v, causal)
+
+
+@pytest.mark.parametrize("d", [32, 64, 128])
+def test_cfg4_outliers_small(d):
+    """Config-4 style large-logit outliers (1% of Q/K entries x20), smaller batch."""
+    cfg = CONFIGS[f"cfg4_d{d}"]
+    q, k, v = generate(cfg, batch=1)
+    _run_and_check(q[:, :4].contiguous(), k[:, :4].contiguous(), v[:, :4].contiguous(), False, cfg.scale)
+
+
+def test_stress_and_structured_modes():
+    """The reference's `stress` and `structured` input modes (input_data.py:33-60)."""
+    # |O| up to ~60 here: the reference's own tolerance for this mode (see tests/parity.py).
+    _run_and_check(*make_stress((1, 2, 384, 128), torch.float16, seed=11), causal=False, atol=2e-2, rtol=2e-2)
+    _run_and_check(*make_structured((2, 2, 256, 64), torch.bfloat16), causal=True)
+
+
+def test_user_scale():
+    q, k, v = make_random((1, 2, 256, 64), torch.float16, seed=3)
+    _run_and_check(q, k, v, causal=True, scale=0.37)
+
+
+def test_cfg2_causal_subset():
+    """Headline config 2 (B8 H32 N4096 d128 bf16 causal): slices 0, 1, 255 vs the oracle."""
+    cfg = CONFIGS["cfg2"]
+    q, k, v = generate(cfg)
+    dev = torch.device("cuda", 0)
+    out, lse = fa.forward(q.to(dev), k.to(dev), v.to(dev), causal=True, return_lse=True)
+    torch.cuda.synchronize(dev)
+    s = cfg.slices
+    flat = lambda t: t.reshape(s, *t.shape[2:])  # noqa: E731
+    for idx in (0, 1, s - 1):
+        ref_o, ref_lse = oracle_attention(flat(q)[idx:idx + 1][None].float().numpy(),
+                                          flat(k)[idx:idx + 1][None].float().numpy(),
+                                          flat(v)[idx:idx + 1][None].float().numpy(), cfg.scale, True)
+        assert compare_output(flat(out)[idx][None, None], ref_o, cfg.dtype)["ok"]
+        assert compare_lse(flat(lse)[idx][None, None], ref_lse)["ok"]
+
+
+def test_strided_bnhd_layout():
+    """[B, N, H, d] memory viewed as [B, H, N, d] (non-contiguous, last dim contiguous)."""
+    q, k, v = make_random((2, 3, 256, 64), torch.bfloat16, seed=21)
+    dev = torch.device("cuda", 0)
+    qs, ks, vs = (t.to(dev).transpose(1, 2).contiguous().transpose(1, 2) for t in (q, k, v))
+    assert not qs.is_contiguous()
+    out, lse = fa.forward(qs, ks, vs, causal=True, return_lse=True)
+    torch.cuda.synchronize(dev)
+    ref_o, ref_lse = oracle_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), 1 / 8, True)
+    assert compare_output(out, ref_o, torch.bfloat16)["ok"]
+    assert compare_lse(lse, ref_lse)["ok"]
+
+
+def test_forward_timed_and_reference_call_shape():
+    """forward(q,k,v) with the reference defaults, forward_timed returns (o, ms)."""
+    q, k, v = make_random((1, 2, 256, 128), torch.float16, seed=5)
+    dev = torch.device("cuda", 0)
+    qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
+    o1 = fa.forward(qd, kd, vd)
+    o2, ms = fa.forward_timed(qd, kd, vd)
+    assert ms > 0.0
+    assert torch.equal(o1, o2)
+    o3 = torch.empty_like(qd)
+    ret, _ = fa.ext_forward(qd, kd, vd, o3, False)
+    assert ret.data_ptr() == o3.data_ptr()
+    assert torch.equal(o3, o1)
+
+
+def test_deterministic_repeat():
+    q, k, v = make_random((2, 4, 1024, 128), torch.bfloat16, seed=9)
+    dev = torch.device("cuda", 0)
+    qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
+    a = fa.forward(qd, kd, vd, causal=True)
+    b = fa.forward(qd, kd, vd, causal=True)
+    assert torch.equal(a, b)
+
+
+def test_full_size_properties_cfg3():
+    """Config 3 (B2 H32 N16384 d128 bf16 causal) at full size, size-independent checks:
+    causal row 0 equals V row 0, every output row is a convex combination of V rows
+    (within [min V, max V] per column), LSE of row 0 equals scale*q0.k0, and a
+    second run is bit-identical."""
+    cfg = CONFIGS["cfg3"]
+    q, k, v = generate(cfg)
+    dev = torch.device("cuda", 0)
+    qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
+    out, lse = fa.forward(qd, kd, vd, causal=True, return_lse=True)
+    out2 = fa.forward(qd, kd, vd, causal=True)
+    torch.cuda.synchronize(dev)
+    assert torch.equal(out, out2)
+    assert torch.allclose(out[:, :, 0].float(), vd[:, :, 0].float(), atol=0, rtol=2 ** -8)
+    vmin = vd.float().amin(dim=2, keepdim=True)
+    vmax = vd.float().amax(dim=2, keepdim=True)
+    of = out.float()
+    assert bool(((of >= vmin - 1e-2) & (of <= vmax + 1e-2)).all())
+    l0 = (qd[:, :, 0].float() * kd[:, :, 0].float()).sum(-1) * cfg.scale
+    assert float((lse[:, :, 0] - l0).abs().max()) < 1e-4 * max(1.0, float(l0.abs().max()))
+    assert bool(torch.isfinite(lse).all())
