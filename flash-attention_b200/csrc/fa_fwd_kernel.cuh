@@ -5,20 +5,25 @@
 // per CTA with sm_80 mma.sync.  Same mathematics (softmax(scale*Q K^T [+causal]) V
 // with the online softmax of src/softmax/online_softmax.cuh:13-252), new machine:
 //
-//  * one persistent CTA per SM; a CTA work unit ("tile") is a pair of 128-row
-//    query tiles Q0, Q1 of one (batch, head) slice, handed out by an atomic
-//    counter in a global workspace (LPT order for causal, grouped by slice so the
-//    K/V of the slices in flight stay in L2);
-//  * warp 8  : TMA producer  - Q0/Q1 once per tile, K_j / V_j through a ring of
+//  * one persistent CTA (512 threads) per SM; a CTA work unit ("tile") is a pair
+//    of 128-row query tiles Q0, Q1 of one (batch, head) slice, handed out by an
+//    atomic counter in a global workspace (heaviest causal tiles first, grouped by
+//    slice so the K/V of the slices in flight stay in L2);
+//  * warp 12 : TMA producer - Q0/Q1 once per tile, K_j / V_j through a ring of
 //              STAGES shared-memory stages (mbarrier full/empty pairs);
-//  * warp 9  : MMA issuer    - tcgen05.mma S_i = Q_i K_j^T (smem x smem -> TMEM)
+//  * warp 13 : MMA issuer   - tcgen05.mma S_i = Q_i K_j^T (smem x smem -> TMEM)
 //              and O_i += P_i V_j (P from TMEM, V from smem, O in TMEM);
 //  * warps 0-3 / 4-7 : softmax warpgroup i for query tile i, one thread per row
-//              (= TMEM lane): tcgen05.ld of the S row, mask, row max, exp2 with the
-//              scale folded in, row sum, P rounded to the input type and written
-//              back into the S columns with tcgen05.st; lazy O rescale (only when
-//              the running max grows by more than 2^8); final 1/l normalise, O
-//              store and logsumexp.
+//              (= TMEM lane): tcgen05.ld of the S row, mask, row max, exp2 with
+//              the scale folded in (part of them on the FMA pipe, see exp2_fma),
+//              row sum, P rounded to the input type and written back over the S
+//              columns with tcgen05.st; lazy O rescale (only when the running max
+//              grows by more than 2^8);
+//  * warps 8-11 : epilogue warpgroup - O_i from TMEM, 1/l normalise, O store and
+//              logsumexp, so the softmax warps go straight on to the next tile;
+//  * warps 14-15 idle.  setmaxnreg gives softmax 184 registers per thread, the
+//    epilogue 80 and the producer / MMA warpgroup 64 (2*128*184 + 128*80 +
+//    128*64 = 64K, the whole register file).
 //
 // TMEM (512 columns x 128 lanes of 32 bit): S0 [0,128) S1 [128,256)
 // O0 [256,256+D) O1 [256+D,256+2D); P_i aliases the first 64 columns of S_i.
@@ -35,6 +40,12 @@
 
 #include "ptx.cuh"
 #include "umma_layout.h"
+
+#ifndef FA_EXP2_FMA_PAIRS
+// Of every 8 column pairs of an unmasked S row, how many take exp2 on the FMA
+// pipe instead of the MUFU unit (0..8).
+#define FA_EXP2_FMA_PAIRS 2
+#endif
 
 namespace fa {
 
@@ -56,14 +67,15 @@ struct KernelParams {
 // Status codes written to KernelParams::status: 0x100 | where.
 enum : int {
   kWaitSched = 1, kWaitQEmpty, kWaitKvEmpty, kWaitQFull, kWaitKvFull, kWaitPFull, kWaitOEmpty,
-  kWaitSFull, kWaitOFull,
+  kWaitSFull, kWaitOFull, kWaitStatsFull, kWaitStatsEmpty,
 };
 
 constexpr int kBlockM = 128;
 constexpr int kBlockN = 128;
-constexpr int kNumThreads = 320;
-constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;
+constexpr int kNumThreads = 512;
+constexpr int kEpilogueWarp0 = 8;
+constexpr int kProducerWarp = 12;
+constexpr int kMmaWarp = 13;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only if the max grew by > 2^8
 
 template <int D>
@@ -74,10 +86,10 @@ struct Cfg {
   static constexpr int STAGES = D == 128 ? 4 : (D == 64 ? 6 : 8);
   static constexpr uint32_t Q_OFF = 0;
   static constexpr uint32_t KV_OFF = 2 * TILE_BYTES;
-  static constexpr uint32_t BAR_OFF = KV_OFF + STAGES * TILE_BYTES;
-  // barriers: sched_full[2] sched_empty[2] q_full[2] q_empty[2] s_full[2] p_full[2]
-  //           o_full[2] o_empty[2] drain[1] kv_full[S] kv_empty[S]
-  static constexpr int NBARS = 17 + 2 * STAGES;
+  static constexpr uint32_t STATS_OFF = KV_OFF + STAGES * TILE_BYTES;  // float2 [wg][slot][row]
+  static constexpr uint32_t BAR_OFF = STATS_OFF + 2 * 2 * 128 * 8;
+  // barrier index layout, see fa_fwd_sm100_kernel
+  static constexpr int NBARS = 25 + 2 * STAGES;
   static constexpr uint32_t MISC_OFF = BAR_OFF + NBARS * 8;  // tmem slot, sched slots, abort flag
   static constexpr uint32_t SMEM_BYTES = MISC_OFF + 64 + 1024;  // + alignment slack
   static constexpr uint32_t TMEM_COLS = 512;
@@ -101,6 +113,13 @@ __device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity, vola
       }
     }
   }
+}
+
+// Warp-uniform bounded wait: every lane polls, the warp agrees on the outcome.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          const KernelParams& p, int where) {
+  const bool ok = bounded_wait(bar, parity, abort_flag, p, where);
+  return __all_sync(0xffffffffu, ok);
 }
 
 // Wait that ignores the abort flag; used only to drain work already in flight.
@@ -128,8 +147,7 @@ __device__ __forceinline__ TileInfo decode_tile(int tile, const KernelParams& p)
   t.b = bh / p.heads;
   t.h = bh - t.b * p.heads;
   t.pair = CAUSAL ? (p.n_pairs - 1 - rank) : rank;
-  const int q0 = t.pair * 256;
-  const int q1 = q0 + 128;
+  const int q1 = t.pair * 256 + 128;
   t.n0 = CAUSAL ? min(2 * t.pair + 1, p.n_kv) : p.n_kv;
   t.n1 = q1 >= p.seq_len ? 0 : (CAUSAL ? min(2 * t.pair + 2, p.n_kv) : p.n_kv);
   return t;
@@ -146,6 +164,52 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   }
 }
 
+// 2^x for two lanes on the FMA pipe (no MUFU).  Cody-Waite style split
+// x = n + f with n = round-to-nearest(x) (obtained by adding 1.5*2^23, which
+// leaves n in the low mantissa bits), f in [-0.5, 0.5]; 2^f from a degree-4
+// polynomial fitted for this kernel by a Remez exchange for minimax relative
+// error on [-0.5, 0.5] (max relative error 2.6e-6); 2^n applied by adding n to
+// the exponent field.  x is clamped to >= -125 so the result stays a normal
+// number; callers use it only for finite x <= 2^8 (unmasked scores).
+__device__ __forceinline__ float2 exp2_fma(float2 x) {
+  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -125.0f);
+  x.y = fmaxf(x.y, -125.0f);
+  const float2 t = add2(x, make_float2(kShift, kShift));
+  const float2 n = add2(t, make_float2(-kShift, -kShift));
+  const float2 f = fma2(n, make_float2(-1.0f, -1.0f), x);
+  float2 q = fma2(make_float2(0.009570102f, 0.009570102f), f, make_float2(0.055917859f, 0.055917859f));
+  q = fma2(q, f, make_float2(0.240247443f, 0.240247443f));
+  q = fma2(q, f, make_float2(0.693121791f, 0.693121791f));
+  q = fma2(q, f, make_float2(0.999999285f, 0.999999285f));
+  float2 r;
+  r.x = __uint_as_float(__float_as_uint(t.x) * 8388608u + __float_as_uint(q.x));
+  r.y = __uint_as_float(__float_as_uint(t.y) * 8388608u + __float_as_uint(q.y));
+  return r;
+}
+
+// S_i = Q_i K^T: D/16 MMAs of K = 16.  Step kk reads bytes kk*32 of each
+// swizzled row, in column chunk (kk*32)/SW (chunks are 128*SW bytes apart).
+template <int D, int KK = 0>
+__device__ __forceinline__ void mma_chain_s(uint32_t d, uint64_t a0, uint64_t b0, uint32_t idesc) {
+  if constexpr (KK < D / 16) {
+    constexpr uint32_t sw = Cfg<D>::SW;
+    constexpr uint32_t off = ((KK * 32u) / sw) * (kBlockM * sw / 16) + ((KK * 32u) % sw) / 16;
+    umma_ss_at<off, KK == 0 ? 0u : 1u>(d, a0, b0, idesc);
+    mma_chain_s<D, KK + 1>(d, a0, b0, idesc);
+  }
+}
+
+// O_i += P_i V: 8 MMAs of K = 16 rows of V; P step kk is TMEM columns
+// [8kk, 8kk+8) of the S_i region (16 16-bit values packed two per column).
+template <int D, int KK = 0>
+__device__ __forceinline__ void mma_chain_pv(uint32_t d, uint32_t a, uint64_t b0, uint32_t idesc, uint32_t acc) {
+  if constexpr (KK < kBlockN / 16) {
+    umma_ts_at<KK * 8u, KK * 16u * Cfg<D>::SW / 16>(d, a, b0, idesc, KK == 0 ? acc : 1u);
+    mma_chain_pv<D, KK + 1>(d, a, b0, idesc, acc);
+  }
+}
+
 template <int D, bool BF16, bool CAUSAL>
 __global__ void __launch_bounds__(kNumThreads, 1)
     fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -156,12 +220,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + C::BAR_OFF;
   auto bar = [&](int i) -> uint32_t { return bar0 + 8u * i; };
-  // barrier indices
-  const uint32_t SCHED_FULL = 0, SCHED_EMPTY = 2, Q_FULL = 4, Q_EMPTY = 6, S_FULL = 8, P_FULL = 10,
-                 O_FULL = 12, O_EMPTY = 14, DRAIN = 16, KV_FULL = 17, KV_EMPTY = 17 + C::STAGES;
+  // barrier indices ([2] = per query tile / ring slot)
+  constexpr int SCHED_FULL = 0, SCHED_EMPTY = 2, Q_FULL = 4, Q_EMPTY = 6, S_FULL = 8, P_FULL = 10,
+                O_FULL = 12, O_EMPTY = 14, DRAIN = 16, STATS_FULL = 17 /* [wg][slot] */,
+                STATS_EMPTY = 21 /* [wg][slot] */, KV_FULL = 25, KV_EMPTY = 25 + C::STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::MISC_OFF);
   volatile int* sched_tile = reinterpret_cast<volatile int*>(smem + C::MISC_OFF + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::MISC_OFF + 32);
+  float2* stats = reinterpret_cast<float2*>(smem + C::STATS_OFF);  // (m*scale*log2e, l)
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -169,13 +235,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar(SCHED_FULL + i), 1);
-      mbar_init(bar(SCHED_EMPTY + i), 1 + 256);
+      mbar_init(bar(SCHED_EMPTY + i), 1 + 256 + 128);  // MMA thread + softmax + epilogue
       mbar_init(bar(Q_FULL + i), 1);
       mbar_init(bar(Q_EMPTY + i), 1);
       mbar_init(bar(S_FULL + i), 1);
       mbar_init(bar(P_FULL + i), 128);
       mbar_init(bar(O_FULL + i), 1);
       mbar_init(bar(O_EMPTY + i), 128);
+    }
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(bar(STATS_FULL + i), 128);
+      mbar_init(bar(STATS_EMPTY + i), 128);
     }
     mbar_init(bar(DRAIN), 1);
     for (int s = 0; s < C::STAGES; ++s) {
@@ -199,16 +269,16 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
 
-  if (warp == kProducerWarp) {
-    // ------------------------------------------------------------ TMA producer
-    if (lane == 0) {
+  if (warp >= kProducerWarp) {
+    setmaxnreg_dec<64>();
+    if (warp == kProducerWarp && lane == 0) {
+      // ---------------------------------------------------------- TMA producer
       const uint64_t pol_kv = l2_policy_evict_last();
       const uint64_t pol_q = l2_policy_evict_first();
       int tile = blockIdx.x;
       uint32_t sched_cnt = 0, kv_cnt = 0, q_cnt[2] = {0, 0};
-      // phase parity of the last arming of each full barrier, for the abort drain
-      uint32_t kv_armed = 0, q_armed = 0;  // bit s: armed and maybe in flight
-      uint32_t kv_par = 0, q_par = 0;      // bit s: parity armed
+      // parity of the last arming of each full barrier, for the abort drain
+      uint32_t kv_armed = 0, q_armed = 0, kv_par = 0, q_par = 0;
       bool ok = true;
       auto load_q = [&](int i, const TileInfo& t) -> bool {
         if (!bounded_wait(bar(Q_EMPTY + i), (q_cnt[i] & 1) ^ 1, abort_flag, p, kWaitQEmpty)) return false;
@@ -264,10 +334,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         for (int i = 0; i < 2; ++i)
           if (q_armed & (1u << i)) drain_wait(bar(Q_FULL + i), (q_par >> i) & 1, 200000000ull);
       }
-    }
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    } else if (warp == kMmaWarp && lane == 0) {
+      // ---------------------------------------------------------- MMA issuer
       constexpr uint32_t idesc_qk = make_idesc_f16(BF16, kBlockM, kBlockN, false, false);
       constexpr uint32_t idesc_pv = make_idesc_f16(BF16, kBlockM, D, false, true);
       uint32_t sched_cnt = 0, kv_cnt = 0, qf_cnt[2] = {0, 0}, pf_cnt[2] = {0, 0}, oe_cnt[2] = {0, 0};
@@ -278,20 +346,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         ++kv_cnt;
         return bounded_wait(bar(KV_FULL + stage), ph, abort_flag, p, kWaitKvFull);
       };
+      // Straight-line MMA chains: each tcgen05.mma of S (K = 16 per instruction)
+      // takes ~64 tensor cycles, so issue must not lag; descriptor offsets are
+      // compile-time constants added inside the asm.
       auto issue_s = [&](int i, uint32_t stage) {
-        const uint32_t qb = sbase + C::Q_OFF + i * C::TILE_BYTES;
-        const uint32_t kb = sbase + C::KV_OFF + stage * C::TILE_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          umma_ss(tmem_base + C::s_col(i), kmajor_desc(qb, kBlockM, C::SW, kk), kmajor_desc(kb, kBlockN, C::SW, kk),
-                  idesc_qk, kk > 0 ? 1u : 0u);
+        const uint64_t a0 = kmajor_desc(sbase + C::Q_OFF + i * C::TILE_BYTES, kBlockM, C::SW, 0);
+        const uint64_t b0 = kmajor_desc(sbase + C::KV_OFF + stage * C::TILE_BYTES, kBlockN, C::SW, 0);
+        mma_chain_s<D>(tmem_base + C::s_col(i), a0, b0, idesc_qk);
       };
       auto issue_pv = [&](int i, uint32_t stage, bool accumulate) {
-        const uint32_t vb = sbase + C::KV_OFF + stage * C::TILE_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < kBlockN / 16; ++kk)
-          umma_ts(tmem_base + C::o_col(i), tmem_base + C::s_col(i) + kk * 8, mnmajor_desc(vb, kBlockN, C::SW, kk),
-                  idesc_pv, (accumulate || kk > 0) ? 1u : 0u);
+        const uint64_t b0 = mnmajor_desc(sbase + C::KV_OFF + stage * C::TILE_BYTES, kBlockN, C::SW, 0);
+        mma_chain_pv<D>(tmem_base + C::o_col(i), tmem_base + C::s_col(i), b0, idesc_pv, accumulate ? 1u : 0u);
       };
       auto wait_p = [&](int i, int j) -> bool {
         if (!bounded_wait(bar(P_FULL + i), pf_cnt[i] & 1, abort_flag, p, kWaitPFull)) return false;
@@ -366,19 +431,78 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       umma_commit(bar(DRAIN));
       drain_wait(bar(DRAIN), 0, 200000000ull);
     }
+  } else if (warp >= kEpilogueWarp0) {
+    setmaxnreg_dec<80>();
+    // ------------------------------------------------------------ epilogue warpgroup
+    const int row_in_tile = threadIdx.x % 128;
+    const uint32_t lane_addr = static_cast<uint32_t>((warp % 4) * 32) << 16;
+    uint32_t sched_cnt = 0, o_cnt[2] = {0, 0}, st_cnt[2] = {0, 0};
+    while (true) {
+      const uint32_t slot = sched_cnt & 1;
+      if (!warp_wait(bar(SCHED_FULL + slot), (sched_cnt >> 1) & 1, abort_flag, p, kWaitSched)) break;
+      const int tile = sched_tile[slot];
+      mbar_arrive(bar(SCHED_EMPTY + slot));
+      ++sched_cnt;
+      if (tile >= p.num_tiles) break;
+      const TileInfo t = decode_tile<CAUSAL>(tile, p);
+      bool failed = false;
+      for (int i = 0; i < 2 && !failed; ++i) {
+        if ((i == 0 ? t.n0 : t.n1) == 0) continue;
+        const uint32_t ss = st_cnt[i] & 1;
+        if (!warp_wait(bar(STATS_FULL + 2 * i + ss), (st_cnt[i] >> 1) & 1, abort_flag, p, kWaitStatsFull) ||
+            !warp_wait(bar(O_FULL + i), o_cnt[i] & 1, abort_flag, p, kWaitOFull)) {
+          failed = true;
+          break;
+        }
+        ++o_cnt[i];
+        ++st_cnt[i];
+        tc_fence_after();
+        const float2 ml = stats[(i * 2 + ss) * 128 + row_in_tile];
+        mbar_arrive(bar(STATS_EMPTY + 2 * i + ss));
+        const float inv_l = 1.f / ml.y;
+        const int row = t.pair * 256 + i * 128 + row_in_tile;
+        const bool row_ok = row < p.seq_len;
+        uint8_t* orow = reinterpret_cast<uint8_t*>(p.O) +
+                        2 * (t.b * p.o_stride_b + t.h * p.o_stride_h + static_cast<int64_t>(row) * p.o_stride_s);
+        const uint32_t o_addr = tmem_base + lane_addr + C::o_col(i);
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          __syncwarp();
+          uint32_t r[32];
+          tmem_ld32(o_addr + c * 32, r);
+          tmem_wait_ld();
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            pk[e] = pack2<BF16>(__uint_as_float(r[2 * e]) * inv_l, __uint_as_float(r[2 * e + 1]) * inv_l);
+          if (row_ok) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              st_global_v4(orow + c * 64 + v * 16, pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(bar(O_EMPTY + i));
+        if (row_ok && p.LSE != nullptr)
+          p.LSE[(static_cast<int64_t>(t.b) * p.heads + t.h) * p.seq_len + row] =
+              (ml.x + log2f(ml.y)) * 0.69314718055994531f;
+      }
+      if (failed) break;
+    }
+    tc_fence_before();
   } else {
+    setmaxnreg_inc<184>();
     // ------------------------------------------------------------ softmax warpgroups
-    const int wg = warp / 4;                      // query tile 0 or 1
-    const int row_in_tile = threadIdx.x % 128;    // = TMEM lane
+    const int wg = warp / 4;                    // query tile 0 or 1
+    const int row_in_tile = threadIdx.x % 128;  // = TMEM lane
     const uint32_t lane_addr = static_cast<uint32_t>((warp % 4) * 32) << 16;
     const uint32_t s_addr = tmem_base + lane_addr + C::s_col(wg);
     const uint32_t o_addr = tmem_base + lane_addr + C::o_col(wg);
-    uint32_t sched_cnt = 0, s_cnt = 0, o_cnt = 0;
+    uint32_t sched_cnt = 0, s_cnt = 0, st_cnt = 0;
     const float sl2 = p.scale_log2;
     while (true) {
       const uint32_t slot = sched_cnt & 1;
-      bool ok = bounded_wait(bar(SCHED_FULL + slot), (sched_cnt >> 1) & 1, abort_flag, p, kWaitSched);
-      if (!__all_sync(0xffffffffu, ok)) break;
+      if (!warp_wait(bar(SCHED_FULL + slot), (sched_cnt >> 1) & 1, abort_flag, p, kWaitSched)) break;
       const int tile = sched_tile[slot];
       mbar_arrive(bar(SCHED_EMPTY + slot));
       ++sched_cnt;
@@ -390,8 +514,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       float m_ref = -INFINITY, l = 0.f;
       bool failed = false;
       for (int j = 0; j < n; ++j) {
-        ok = bounded_wait(bar(S_FULL + wg), s_cnt & 1, abort_flag, p, kWaitSFull);
-        if (!__all_sync(0xffffffffu, ok)) { failed = true; break; }
+        if (!warp_wait(bar(S_FULL + wg), s_cnt & 1, abort_flag, p, kWaitSFull)) { failed = true; break; }
         ++s_cnt;
         tc_fence_after();
         float s[kBlockN];
@@ -403,87 +526,106 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(r[e]);
         }
         tmem_wait_ld();
-        if (j == n - 1 && (CAUSAL || (p.seq_len % kBlockN) != 0)) {
+        const bool masked = j == n - 1 && (CAUSAL || (p.seq_len % kBlockN) != 0);
+        if (masked) {
           const int k0 = j * kBlockN;
           int lim = p.seq_len - 1 - k0;
           if (CAUSAL) lim = min(lim, row - k0);
 #pragma unroll
           for (int c = 0; c < kBlockN; ++c) s[c] = c > lim ? -INFINITY : s[c];
         }
-        float mt = s[0];
+        // row max: 8 independent 3-input max chains, then a small tree
+        float mx[8];
 #pragma unroll
-        for (int c = 1; c < kBlockN; ++c) mt = fmaxf(mt, s[c]);
+        for (int k = 0; k < 8; ++k) {
+          mx[k] = fmax3(s[16 * k], s[16 * k + 1], s[16 * k + 2]);
+#pragma unroll
+          for (int e = 3; e < 15; e += 2) mx[k] = fmax3(mx[k], s[16 * k + e], s[16 * k + e + 1]);
+          mx[k] = fmaxf(mx[k], s[16 * k + 15]);
+        }
+        const float mt = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
         const float m_new = fmaxf(m_ref, mt);
+        // Lazy rescale: keep the old reference max unless the row max grew by
+        // more than 2^8 (then O and l are scaled by alpha, after P is written).
+        float alpha = 1.f;
+        bool rescale_warp = false;
         if (j == 0) {
           m_ref = m_new;
         } else {
           const bool need = (m_new - m_ref) * sl2 > kRescaleThreshold;
-          if (__any_sync(0xffffffffu, need)) {
-            const float alpha = need ? ex2_approx((m_ref - m_new) * sl2) : 1.f;
-            if (need) {
-              l *= alpha;
-              m_ref = m_new;
-            }
-#pragma unroll 1
-            for (int c = 0; c < D / 32; ++c) {
-              uint32_t r[32];
-              tmem_ld32(o_addr + c * 32, r);
-              tmem_wait_ld();
-#pragma unroll
-              for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-              tmem_st32(o_addr + c * 32, r);
-            }
+          rescale_warp = __any_sync(0xffffffffu, need);
+          if (need) {
+            alpha = ex2_approx((m_ref - m_new) * sl2);
+            l *= alpha;
+            m_ref = m_new;
           }
         }
         const float mc = m_ref == -INFINITY ? 0.f : m_ref * sl2;
-        float lsum = 0.f;
+        const float2 scale2 = make_float2(sl2, sl2);
+        const float2 neg_mc = make_float2(-mc, -mc);
+        float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+        if (masked) {
 #pragma unroll
-        for (int c = 0; c < kBlockN / 64; ++c) {
-          uint32_t pk[32];
+          for (int c = 0; c < kBlockN / 64; ++c) {
+            uint32_t pk[32];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float p0 = ex2_approx(fmaf(s[c * 64 + 2 * e], sl2, -mc));
-            const float p1 = ex2_approx(fmaf(s[c * 64 + 2 * e + 1], sl2, -mc));
-            lsum += p0 + p1;
-            pk[e] = pack2<BF16>(p0, p1);
+            for (int e = 0; e < 32; ++e) {
+              const float2 x = fma2(make_float2(s[c * 64 + 2 * e], s[c * 64 + 2 * e + 1]), scale2, neg_mc);
+              const float2 pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+              acc[e & 3] = add2(acc[e & 3], pp);
+              pk[e] = pack2<BF16>(pp.x, pp.y);
+            }
+            tmem_st32(s_addr + c * 32, pk);
           }
-          tmem_st32(s_addr + c * 32, pk);
+        } else {
+#pragma unroll
+          for (int c = 0; c < kBlockN / 64; ++c) {
+            uint32_t pk[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const float2 x = fma2(make_float2(s[c * 64 + 2 * e], s[c * 64 + 2 * e + 1]), scale2, neg_mc);
+              float2 pp;
+              if ((e & 7) < FA_EXP2_FMA_PAIRS) {
+                pp = exp2_fma(x);
+              } else {
+                pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+              }
+              acc[e & 3] = add2(acc[e & 3], pp);
+              pk[e] = pack2<BF16>(pp.x, pp.y);
+            }
+            tmem_st32(s_addr + c * 32, pk);
+          }
         }
-        l += lsum;
+        const float2 a = add2(add2(acc[0], acc[1]), add2(acc[2], acc[3]));
+        l += a.x + a.y;
+        if (rescale_warp) {
+          // O_i(j-1) is complete: the commit that signalled S_i(j) covers PV_i(j-1).
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(o_addr + c * 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+            tmem_st32(o_addr + c * 32, r);
+          }
+        }
+        if (j == n - 1) {
+          // Hand (m, l) of this row to the epilogue warpgroup.
+          const uint32_t ss = st_cnt & 1;
+          if (!warp_wait(bar(STATS_EMPTY + 2 * wg + ss), ((st_cnt >> 1) & 1) ^ 1, abort_flag, p, kWaitStatsEmpty)) {
+            failed = true;
+            break;
+          }
+          stats[(wg * 2 + ss) * 128 + row_in_tile] = make_float2(mc, l);
+          mbar_arrive(bar(STATS_FULL + 2 * wg + ss));
+          ++st_cnt;
+        }
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(bar(P_FULL + wg));
       }
       if (failed) break;
-      ok = bounded_wait(bar(O_FULL + wg), o_cnt & 1, abort_flag, p, kWaitOFull);
-      if (!__all_sync(0xffffffffu, ok)) break;
-      ++o_cnt;
-      tc_fence_after();
-      const float inv_l = 1.f / l;
-      const bool row_ok = row < p.seq_len;
-      uint8_t* orow = reinterpret_cast<uint8_t*>(p.O) +
-                      2 * (t.b * p.o_stride_b + t.h * p.o_stride_h + static_cast<int64_t>(row) * p.o_stride_s);
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        __syncwarp();
-        uint32_t r[32];
-        tmem_ld32(o_addr + c * 32, r);
-        tmem_wait_ld();
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e)
-          pk[e] = pack2<BF16>(__uint_as_float(r[2 * e]) * inv_l, __uint_as_float(r[2 * e + 1]) * inv_l);
-        if (row_ok) {
-#pragma unroll
-          for (int v = 0; v < 4; ++v) st_global_v4(orow + c * 64 + v * 16, pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
-        }
-      }
-      if (row_ok && p.LSE != nullptr) {
-        const float lse2 = (m_ref == -INFINITY ? 0.f : m_ref * sl2) + log2f(l);
-        p.LSE[(static_cast<int64_t>(t.b) * p.heads + t.h) * p.seq_len + row] = lse2 * 0.69314718055994531f;
-      }
-      tc_fence_before();
-      mbar_arrive(bar(O_EMPTY + wg));
     }
     tc_fence_before();
   }

@@ -131,6 +131,33 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
       : "memory");
 }
 
+// One tcgen05.mma (kind::f16, A and B from smem descriptors) whose descriptors
+// are a0 + OFF and b0 + OFF (start-address field, 16-byte units).  The add is
+// inside the asm, so unrolled chains of these keep only a0 / b0 live.
+template <uint32_t OFF, uint32_t ACC>
+__device__ __forceinline__ void umma_ss_at(uint32_t d_tmem, uint64_t a0, uint64_t b0, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .b64 ra, rb;\n\t.reg .pred p;\n\t"
+      "add.s64 ra, %1, %3;\n\tadd.s64 rb, %2, %3;\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], ra, rb, %4, p;\n\t}" ::"r"(d_tmem),
+      "l"(a0), "l"(b0), "n"(OFF), "r"(idesc), "n"(ACC)
+      : "memory");
+}
+
+// One tcgen05.mma with A from TMEM column a_tmem + ACOL and B = b0 + BOFF.
+template <uint32_t ACOL, uint32_t BOFF>
+__device__ __forceinline__ void umma_ts_at(uint32_t d_tmem, uint32_t a_tmem, uint64_t b0, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .b64 rb;\n\t.reg .b32 ra;\n\t.reg .pred p;\n\t"
+      "add.s32 ra, %1, %3;\n\tadd.s64 rb, %2, %4;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [ra], rb, %5, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b0), "n"(ACOL), "n"(BOFF), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive on `bar` once every tcgen05 op issued so far by this thread has completed.
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
@@ -170,6 +197,49 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 #undef FA_W32
+
+// ---------------------------------------------------------------- register budget
+
+// Warpgroup-collective: raise / lower this warpgroup's per-thread register limit.
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// ---------------------------------------------------------------- fp32 helpers (sm_100)
+
+// Three-input maximum.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Packed two-lane fp32 fused multiply-add: (a.x*b.x + c.x, a.y*b.y + c.y).
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+// Packed two-lane fp32 add.
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
 
 // ---------------------------------------------------------------- misc
 
