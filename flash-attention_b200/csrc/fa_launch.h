@@ -18,6 +18,9 @@ struct LaunchSpec {
   bool causal;
 };
 
+// Sets the message fa_last_error() returns on this host thread.
+void set_last_error(const char* msg);
+
 cudaError_t launch_d32(const LaunchSpec& s);
 cudaError_t launch_d64(const LaunchSpec& s);
 cudaError_t launch_d128(const LaunchSpec& s);

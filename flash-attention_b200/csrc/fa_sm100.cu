@@ -117,6 +117,10 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 }  // namespace
 
+namespace fa {
+void set_last_error(const char* msg) { g_last_error = msg; }
+}  // namespace fa
+
 extern "C" {
 
 size_t fa_fwd_workspace_bytes(void) { return 256; }

@@ -93,6 +93,18 @@ typedef struct fa_fwd_params {
  * (a cudaStream_t; NULL = legacy default stream).  Asynchronous. */
 FA_API int fa_fwd_sm100(const fa_fwd_params* params, void* stream);
 
+/* Same computation as fa_fwd_sm100, for callers that cannot allocate device
+ * memory (code running during CUDA-graph capture, runtimes whose memory pool
+ * forbids outside allocations, plug-in hosts that pass only input and output
+ * buffers).  No counterpart in the reference.  params->workspace must be NULL:
+ * the scheduler's scratch is a fixed 256-byte array inside this library's device
+ * memory (one per GPU, held until the process exits), cleared with
+ * cudaMemsetAsync before every launch.  No cudaMalloc / cudaFree is called.  The
+ * first call on a device looks up the array's address (cudaGetSymbolAddress)
+ * and must therefore come before any stream capture.  All calls on a device
+ * share the array: calls whose kernels overlap on the GPU race on it. */
+FA_API int fa_fwd_sm100_noalloc(const fa_fwd_params* params, void* stream);
+
 /* Dynamic shared memory one CTA of the kernel uses for this head_dim / dtype
  * (the reference's forward_smem_bytes<Cfg>(), src/utils/util_func.cuh:12-21).
  * Returns 0 for an unsupported combination. */
