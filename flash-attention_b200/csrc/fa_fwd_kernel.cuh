@@ -191,22 +191,23 @@ __device__ __forceinline__ float2 exp2_fma(float2 x) {
 // S_i = Q_i K^T: D/16 MMAs of K = 16.  Step kk reads bytes kk*32 of each
 // swizzled row, in column chunk (kk*32)/SW (chunks are 128*SW bytes apart).
 template <int D, int KK = 0>
-__device__ __forceinline__ void mma_chain_s(uint32_t d, uint64_t a0, uint64_t b0, uint32_t idesc) {
+__device__ __forceinline__ void mma_chain_s(uint32_t d, uint32_t a_lo, uint32_t b_lo, uint32_t hi, uint32_t idesc) {
   if constexpr (KK < D / 16) {
     constexpr uint32_t sw = Cfg<D>::SW;
     constexpr uint32_t off = ((KK * 32u) / sw) * (kBlockM * sw / 16) + ((KK * 32u) % sw) / 16;
-    umma_ss_at<off, KK == 0 ? 0u : 1u>(d, a0, b0, idesc);
-    mma_chain_s<D, KK + 1>(d, a0, b0, idesc);
+    umma_ss_at<off, KK == 0 ? 0u : 1u>(d, a_lo, b_lo, hi, idesc);
+    mma_chain_s<D, KK + 1>(d, a_lo, b_lo, hi, idesc);
   }
 }
 
 // O_i += P_i V: 8 MMAs of K = 16 rows of V; P step kk is TMEM columns
 // [8kk, 8kk+8) of the S_i region (16 16-bit values packed two per column).
 template <int D, int KK = 0>
-__device__ __forceinline__ void mma_chain_pv(uint32_t d, uint32_t a, uint64_t b0, uint32_t idesc, uint32_t acc) {
+__device__ __forceinline__ void mma_chain_pv(uint32_t d, uint32_t a, uint32_t b_lo, uint32_t hi, uint32_t idesc,
+                                             uint32_t acc) {
   if constexpr (KK < kBlockN / 16) {
-    umma_ts_at<KK * 8u, KK * 16u * Cfg<D>::SW / 16>(d, a, b0, idesc, KK == 0 ? acc : 1u);
-    mma_chain_pv<D, KK + 1>(d, a, b0, idesc, acc);
+    umma_ts_at<KK * 8u, KK * 16u * Cfg<D>::SW / 16>(d, a, b_lo, hi, idesc, KK == 0 ? acc : 1u);
+    mma_chain_pv<D, KK + 1>(d, a, b_lo, hi, idesc, acc);
   }
 }
 
@@ -346,17 +347,23 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         ++kv_cnt;
         return bounded_wait(bar(KV_FULL + stage), ph, abort_flag, p, kWaitKvFull);
       };
-      // Straight-line MMA chains: each tcgen05.mma of S (K = 16 per instruction)
-      // takes ~64 tensor cycles, so issue must not lag; descriptor offsets are
-      // compile-time constants added inside the asm.
+      // Descriptor words: the high word (stride offset, version, swizzle) is the
+      // same for every tile of this kernel; low words step by whole tiles.
+      constexpr uint64_t kdesc0 = kmajor_desc(0, kBlockM, C::SW, 0);
+      constexpr uint64_t vdesc0 = mnmajor_desc(0, kBlockN, C::SW, 0);
+      constexpr uint32_t k_hi = static_cast<uint32_t>(kdesc0 >> 32);
+      constexpr uint32_t v_hi = static_cast<uint32_t>(vdesc0 >> 32);
+      const uint32_t q_lo0 = static_cast<uint32_t>(kdesc0) + ((sbase + C::Q_OFF) >> 4);
+      const uint32_t k_lo0 = static_cast<uint32_t>(kdesc0) + ((sbase + C::KV_OFF) >> 4);
+      const uint32_t v_lo0 = static_cast<uint32_t>(vdesc0) + ((sbase + C::KV_OFF) >> 4);
+      constexpr uint32_t kTileUnits = C::TILE_BYTES >> 4;
       auto issue_s = [&](int i, uint32_t stage) {
-        const uint64_t a0 = kmajor_desc(sbase + C::Q_OFF + i * C::TILE_BYTES, kBlockM, C::SW, 0);
-        const uint64_t b0 = kmajor_desc(sbase + C::KV_OFF + stage * C::TILE_BYTES, kBlockN, C::SW, 0);
-        mma_chain_s<D>(tmem_base + C::s_col(i), a0, b0, idesc_qk);
+        mma_chain_s<D>(tmem_base + C::s_col(i), q_lo0 + i * kTileUnits, k_lo0 + stage * kTileUnits, k_hi,
+                       idesc_qk);
       };
       auto issue_pv = [&](int i, uint32_t stage, bool accumulate) {
-        const uint64_t b0 = mnmajor_desc(sbase + C::KV_OFF + stage * C::TILE_BYTES, kBlockN, C::SW, 0);
-        mma_chain_pv<D>(tmem_base + C::o_col(i), tmem_base + C::s_col(i), b0, idesc_pv, accumulate ? 1u : 0u);
+        mma_chain_pv<D>(tmem_base + C::o_col(i), tmem_base + C::s_col(i), v_lo0 + stage * kTileUnits, v_hi, idesc_pv,
+                        accumulate ? 1u : 0u);
       };
       auto wait_p = [&](int i, int j) -> bool {
         if (!bounded_wait(bar(P_FULL + i), pf_cnt[i] & 1, abort_flag, p, kWaitPFull)) return false;

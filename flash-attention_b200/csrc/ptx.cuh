@@ -131,30 +131,35 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
       : "memory");
 }
 
-// One tcgen05.mma (kind::f16, A and B from smem descriptors) whose descriptors
-// are a0 + OFF and b0 + OFF (start-address field, 16-byte units).  The add is
-// inside the asm, so unrolled chains of these keep only a0 / b0 live.
+// One tcgen05.mma (kind::f16, A and B from smem descriptors).  A descriptor is
+// passed as its low word (start address | leading byte offset) and its high word
+// (stride byte offset | version | layout); step OFF of a chain adds OFF to the
+// start address (16-byte units) of both.  The low-word add cannot carry: shared
+// memory addresses stay below 2^18 bytes.  Keeping the add 32-bit and the high
+// word shared keeps the issuing thread's instruction count per MMA small.
 template <uint32_t OFF, uint32_t ACC>
-__device__ __forceinline__ void umma_ss_at(uint32_t d_tmem, uint64_t a0, uint64_t b0, uint32_t idesc) {
+__device__ __forceinline__ void umma_ss_at(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t hi,
+                                           uint32_t idesc) {
   asm volatile(
-      "{\n\t.reg .b64 ra, rb;\n\t.reg .pred p;\n\t"
-      "add.s64 ra, %1, %3;\n\tadd.s64 rb, %2, %3;\n\t"
-      "setp.ne.b32 p, %5, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], ra, rb, %4, p;\n\t}" ::"r"(d_tmem),
-      "l"(a0), "l"(b0), "n"(OFF), "r"(idesc), "n"(ACC)
+      "{\n\t.reg .b32 al, bl;\n\t.reg .b64 ra, rb;\n\t.reg .pred p;\n\t"
+      "add.u32 al, %1, %4;\n\tadd.u32 bl, %2, %4;\n\t"
+      "mov.b64 ra, {al, %3};\n\tmov.b64 rb, {bl, %3};\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], ra, rb, %5, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_lo), "r"(b_lo), "r"(hi), "n"(OFF), "r"(idesc), "n"(ACC)
       : "memory");
 }
 
-// One tcgen05.mma with A from TMEM column a_tmem + ACOL and B = b0 + BOFF.
+// One tcgen05.mma with A from TMEM column a_tmem + ACOL and B = (b_lo + BOFF, hi).
 template <uint32_t ACOL, uint32_t BOFF>
-__device__ __forceinline__ void umma_ts_at(uint32_t d_tmem, uint32_t a_tmem, uint64_t b0, uint32_t idesc,
-                                           uint32_t accumulate) {
+__device__ __forceinline__ void umma_ts_at(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t hi,
+                                           uint32_t idesc, uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .b64 rb;\n\t.reg .b32 ra;\n\t.reg .pred p;\n\t"
-      "add.s32 ra, %1, %3;\n\tadd.s64 rb, %2, %4;\n\t"
-      "setp.ne.b32 p, %6, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [ra], rb, %5, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b0), "n"(ACOL), "n"(BOFF), "r"(idesc), "r"(accumulate)
+      "{\n\t.reg .b32 ra, bl;\n\t.reg .b64 rb;\n\t.reg .pred p;\n\t"
+      "add.u32 ra, %1, %4;\n\tadd.u32 bl, %2, %5;\n\tmov.b64 rb, {bl, %3};\n\t"
+      "setp.ne.b32 p, %7, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [ra], rb, %6, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(hi), "n"(ACOL), "n"(BOFF), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
