@@ -9,8 +9,11 @@
 //    of 128-row query tiles Q0, Q1 of one (batch, head) slice, handed out by an
 //    atomic counter in a global workspace (heaviest causal tiles first, grouped by
 //    slice so the K/V of the slices in flight stay in L2);
-//  * warp 12 : TMA producer - Q0/Q1 once per tile, K_j / V_j through a ring of
-//              STAGES shared-memory stages (mbarrier full/empty pairs);
+//  * warp 12 : TMA producer - Q0/Q1 once per tile, then K/V tiles through a
+//              ring of STAGES shared-memory slots used two at a time: slot pair
+//              {V_j, K_j+1} (K_0 alone at a tile's start, V_n-1 alone at its end)
+//              behind one full and one empty mbarrier, so the MMA thread acquires
+//              and releases once per key block;
 //  * warp 13 : MMA issuer   - tcgen05.mma S_i = Q_i K_j^T (smem x smem -> TMEM)
 //              and O_i += P_i V_j (P from TMEM, V from smem, O in TMEM);
 //  * warps 0-3 / 4-7 : softmax warpgroup i for query tile i, one thread per row
@@ -83,13 +86,14 @@ struct Cfg {
   static constexpr uint32_t SW = swizzle_bytes(D);
   static constexpr int CHUNKS = D * 2 / SW;
   static constexpr uint32_t TILE_BYTES = kBlockM * D * 2;  // Q, K and V tiles are all 128 x D
-  static constexpr int STAGES = D == 128 ? 4 : (D == 64 ? 6 : 8);
+  static constexpr int STAGES = D == 128 ? 4 : (D == 64 ? 6 : 8);  // K/V tile slots
+  static constexpr int NPAIRS = STAGES / 2;                           // slot pairs
   static constexpr uint32_t Q_OFF = 0;
   static constexpr uint32_t KV_OFF = 2 * TILE_BYTES;
   static constexpr uint32_t STATS_OFF = KV_OFF + STAGES * TILE_BYTES;  // float2 [wg][slot][row]
   static constexpr uint32_t BAR_OFF = STATS_OFF + 2 * 2 * 128 * 8;
   // barrier index layout, see fa_fwd_sm100_kernel
-  static constexpr int NBARS = 25 + 2 * STAGES;
+  static constexpr int NBARS = 25 + 2 * NPAIRS;
   static constexpr uint32_t MISC_OFF = BAR_OFF + NBARS * 8;  // tmem slot, sched slots, abort flag
   static constexpr uint32_t SMEM_BYTES = MISC_OFF + 64 + 1024;  // + alignment slack
   static constexpr uint32_t TMEM_COLS = 512;
@@ -224,7 +228,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   // barrier indices ([2] = per query tile / ring slot)
   constexpr int SCHED_FULL = 0, SCHED_EMPTY = 2, Q_FULL = 4, Q_EMPTY = 6, S_FULL = 8, P_FULL = 10,
                 O_FULL = 12, O_EMPTY = 14, DRAIN = 16, STATS_FULL = 17 /* [wg][slot] */,
-                STATS_EMPTY = 21 /* [wg][slot] */, KV_FULL = 25, KV_EMPTY = 25 + C::STAGES;
+                STATS_EMPTY = 21 /* [wg][slot] */, KV_FULL = 25 /* [pair] */, KV_EMPTY = 25 + C::NPAIRS;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::MISC_OFF);
   volatile int* sched_tile = reinterpret_cast<volatile int*>(smem + C::MISC_OFF + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::MISC_OFF + 32);
@@ -249,7 +253,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       mbar_init(bar(STATS_EMPTY + i), 128);
     }
     mbar_init(bar(DRAIN), 1);
-    for (int s = 0; s < C::STAGES; ++s) {
+    for (int s = 0; s < C::NPAIRS; ++s) {
       mbar_init(bar(KV_FULL + s), 1);
       mbar_init(bar(KV_EMPTY + s), 1);
     }
@@ -295,18 +299,28 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         ++q_cnt[i];
         return true;
       };
-      auto load_kv = [&](const CUtensorMap* m, int j, const TileInfo& t) -> bool {
-        const uint32_t s = kv_cnt % C::STAGES;
-        const uint32_t ph = (kv_cnt / C::STAGES) & 1;
-        if (!bounded_wait(bar(KV_EMPTY + s), ph ^ 1, abort_flag, p, kWaitKvEmpty)) return false;
-        const uint32_t fb = bar(KV_FULL + s);
-        mbar_arrive_expect_tx(fb, C::TILE_BYTES);
-        kv_armed |= 1u << s;
-        kv_par = (kv_par & ~(1u << s)) | (ph << s);
-        const uint32_t dst = sbase + C::KV_OFF + s * C::TILE_BYTES;
+      // Loads V rows [128 v, 128 v + 128) into the pair's first slot and K rows
+      // [128 k, 128 k + 128) into its second (v or k < 0: that slot stays unused).
+      auto load_pair = [&](int v, int k, const TileInfo& t) -> bool {
+        const uint32_t pr = kv_cnt % C::NPAIRS;
+        const uint32_t ph = (kv_cnt / C::NPAIRS) & 1;
+        if (!bounded_wait(bar(KV_EMPTY + pr), ph ^ 1, abort_flag, p, kWaitKvEmpty)) return false;
+        const uint32_t fb = bar(KV_FULL + pr);
+        mbar_arrive_expect_tx(fb, (v >= 0 ? C::TILE_BYTES : 0u) + (k >= 0 ? C::TILE_BYTES : 0u));
+        kv_armed |= 1u << pr;
+        kv_par = (kv_par & ~(1u << pr)) | (ph << pr);
+        const uint32_t dst = sbase + C::KV_OFF + 2 * pr * C::TILE_BYTES;
+        if (v >= 0) {
 #pragma unroll
-        for (int c = 0; c < C::CHUNKS; ++c)
-          tma_load_4d(dst + c * kBlockN * C::SW, m, fb, c * int(C::SW / 2), j * kBlockN, t.h, t.b, pol_kv);
+          for (int c = 0; c < C::CHUNKS; ++c)
+            tma_load_4d(dst + c * kBlockN * C::SW, &tmV, fb, c * int(C::SW / 2), v * kBlockN, t.h, t.b, pol_kv);
+        }
+        if (k >= 0) {
+#pragma unroll
+          for (int c = 0; c < C::CHUNKS; ++c)
+            tma_load_4d(dst + C::TILE_BYTES + c * kBlockN * C::SW, &tmK, fb, c * int(C::SW / 2), k * kBlockN, t.h,
+                        t.b, pol_kv);
+        }
         ++kv_cnt;
         return true;
       };
@@ -320,17 +334,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         const int next = atomicAdd(p.tile_counter, 1) + static_cast<int>(gridDim.x);
         const TileInfo t = decode_tile<CAUSAL>(tile, p);
         const int nmax = max(t.n0, t.n1);
-        ok = load_q(0, t) && load_kv(&tmK, 0, t);
+        ok = load_q(0, t) && load_pair(-1, 0, t);
         if (ok && t.n1 > 0) ok = load_q(1, t);
-        for (int j = 0; ok && j < nmax; ++j) {
-          ok = load_kv(&tmV, j, t);
-          if (ok && j + 1 < nmax) ok = load_kv(&tmK, j + 1, t);
-        }
+        for (int j = 0; ok && j < nmax; ++j) ok = load_pair(j, j + 1 < nmax ? j + 1 : -1, t);
         tile = next;
       }
       if (*abort_flag) {
         // Let every copy this thread started land before the CTA exits.
-        for (int s = 0; s < C::STAGES; ++s)
+        for (int s = 0; s < C::NPAIRS; ++s)
           if (kv_armed & (1u << s)) drain_wait(bar(KV_FULL + s), (kv_par >> s) & 1, 200000000ull);
         for (int i = 0; i < 2; ++i)
           if (q_armed & (1u << i)) drain_wait(bar(Q_FULL + i), (q_par >> i) & 1, 200000000ull);
@@ -341,11 +352,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       constexpr uint32_t idesc_pv = make_idesc_f16(BF16, kBlockM, D, false, true);
       uint32_t sched_cnt = 0, kv_cnt = 0, qf_cnt[2] = {0, 0}, pf_cnt[2] = {0, 0}, oe_cnt[2] = {0, 0};
       bool ok = true;
-      auto acquire = [&](uint32_t& stage) -> bool {
-        stage = kv_cnt % C::STAGES;
-        const uint32_t ph = (kv_cnt / C::STAGES) & 1;
+      // Slot pair pr holds V in slot 2 pr and K in slot 2 pr + 1.
+      auto acquire = [&](uint32_t& pr) -> bool {
+        pr = kv_cnt % C::NPAIRS;
+        const uint32_t ph = (kv_cnt / C::NPAIRS) & 1;
         ++kv_cnt;
-        return bounded_wait(bar(KV_FULL + stage), ph, abort_flag, p, kWaitKvFull);
+        return bounded_wait(bar(KV_FULL + pr), ph, abort_flag, p, kWaitKvFull);
       };
       // Descriptor words: the high word (stride offset, version, swizzle) is the
       // same for every tile of this kernel; low words step by whole tiles.
@@ -384,36 +396,32 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         if (tile >= p.num_tiles) break;
         const TileInfo t = decode_tile<CAUSAL>(tile, p);
         const int n0 = t.n0, n1 = t.n1, nmax = max(n0, n1);
-        uint32_t sk;
-        ok = acquire(sk) && bounded_wait(bar(Q_FULL + 0), qf_cnt[0] & 1, abort_flag, p, kWaitQFull);
+        uint32_t pk;
+        ok = acquire(pk) && bounded_wait(bar(Q_FULL + 0), qf_cnt[0] & 1, abort_flag, p, kWaitQFull);
         if (!ok) break;
         ++qf_cnt[0];
         tc_fence_after();
-        issue_s(0, sk);
+        issue_s(0, 2 * pk + 1);
         umma_commit(bar(S_FULL + 0));
         if (n0 == 1) umma_commit(bar(Q_EMPTY + 0));
         if (n1 > 0) {
           if (!bounded_wait(bar(Q_FULL + 1), qf_cnt[1] & 1, abort_flag, p, kWaitQFull)) break;
           ++qf_cnt[1];
           tc_fence_after();
-          issue_s(1, sk);
+          issue_s(1, 2 * pk + 1);
           umma_commit(bar(S_FULL + 1));
           if (n1 == 1) umma_commit(bar(Q_EMPTY + 1));
         }
-        umma_commit(bar(KV_EMPTY + sk));
+        umma_commit(bar(KV_EMPTY + pk));
         for (int j = 0; j < nmax; ++j) {
-          uint32_t sv, skn = 0;
-          if (!acquire(sv)) { ok = false; break; }
+          uint32_t pj;
+          if (!acquire(pj)) { ok = false; break; }
           tc_fence_after();
-          const bool has_next = j + 1 < nmax;
+          const uint32_t sv = 2 * pj, skn = 2 * pj + 1;
           if (j < n0) {
             if (!wait_p(0, j)) { ok = false; break; }
             issue_pv(0, sv, j > 0);
             if (j == n0 - 1) umma_commit(bar(O_FULL + 0));
-          }
-          if (has_next) {
-            if (!acquire(skn)) { ok = false; break; }
-            tc_fence_after();
           }
           if (j + 1 < n0) {
             issue_s(0, skn);
@@ -430,8 +438,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             umma_commit(bar(S_FULL + 1));
             if (j + 2 == n1) umma_commit(bar(Q_EMPTY + 1));
           }
-          umma_commit(bar(KV_EMPTY + sv));
-          if (has_next) umma_commit(bar(KV_EMPTY + skn));
+          umma_commit(bar(KV_EMPTY + pj));
         }
       }
       // Every MMA issued by this thread completes before TMEM and smem go away.
