@@ -15,7 +15,8 @@
 //              behind one full and one empty mbarrier, so the MMA thread acquires
 //              and releases once per key block;
 //  * warp 13 : MMA issuer   - tcgen05.mma S_i = Q_i K_j^T (smem x smem -> TMEM)
-//              and O_i += P_i V_j (P from TMEM, V from smem, O in TMEM);
+//              and O_i += P_i V_j (P from TMEM, V from smem, O in TMEM); the
+//              warp runs converged and elect.sync picks the issuing lane;
 //  * warps 0-3 / 4-7 : softmax warpgroup i for query tile i, one thread per row
 //              (= TMEM lane): tcgen05.ld of the S row, mask, row max, exp2 with
 //              the scale folded in (part of them on the FMA pipe, see exp2_fma),
@@ -346,8 +347,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         for (int i = 0; i < 2; ++i)
           if (q_armed & (1u << i)) drain_wait(bar(Q_FULL + i), (q_par >> i) & 1, 200000000ull);
       }
-    } else if (warp == kMmaWarp && lane == 0) {
+    } else if (warp == kMmaWarp) {
       // ---------------------------------------------------------- MMA issuer
+      // All 32 lanes run this loop (see the elect.sync wrappers in ptx.cuh).  A
+      // wait's try_wait is one instruction for the whole warp, so every lane sees
+      // the same outcome and the loop stays converged; single arrivals come from
+      // lane 0.
       constexpr uint32_t idesc_qk = make_idesc_f16(BF16, kBlockM, kBlockN, false, false);
       constexpr uint32_t idesc_pv = make_idesc_f16(BF16, kBlockM, D, false, true);
       uint32_t sched_cnt = 0, kv_cnt = 0, qf_cnt[2] = {0, 0}, pf_cnt[2] = {0, 0}, oe_cnt[2] = {0, 0};
@@ -391,7 +396,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         const uint32_t slot = sched_cnt & 1;
         if (!bounded_wait(bar(SCHED_FULL + slot), (sched_cnt >> 1) & 1, abort_flag, p, kWaitSched)) break;
         const int tile = sched_tile[slot];
-        mbar_arrive(bar(SCHED_EMPTY + slot));
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(SCHED_EMPTY + slot));
         ++sched_cnt;
         if (tile >= p.num_tiles) break;
         const TileInfo t = decode_tile<CAUSAL>(tile, p);

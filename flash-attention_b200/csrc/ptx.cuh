@@ -131,21 +131,26 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
       : "memory");
 }
 
+// The MMA warp runs converged: every lane executes the loop (so descriptors and
+// addresses are warp-uniform and stay on the uniform datapath) and each tcgen05
+// instruction below is issued by the lane elect.sync picks.  With the full mask
+// that is always the lowest lane, so all MMAs and commits come from one thread,
+// as tcgen05.commit's completion tracking requires.
+
 // One tcgen05.mma (kind::f16, A and B from smem descriptors).  A descriptor is
 // passed as its low word (start address | leading byte offset) and its high word
 // (stride byte offset | version | layout); step OFF of a chain adds OFF to the
 // start address (16-byte units) of both.  The low-word add cannot carry: shared
-// memory addresses stay below 2^18 bytes.  Keeping the add 32-bit and the high
-// word shared keeps the issuing thread's instruction count per MMA small.
+// memory addresses stay below 2^18 bytes.
 template <uint32_t OFF, uint32_t ACC>
 __device__ __forceinline__ void umma_ss_at(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t hi,
                                            uint32_t idesc) {
   asm volatile(
-      "{\n\t.reg .b32 al, bl;\n\t.reg .b64 ra, rb;\n\t.reg .pred p;\n\t"
+      "{\n\t.reg .b32 al, bl;\n\t.reg .b64 ra, rb;\n\t.reg .pred p, e;\n\t"
       "add.u32 al, %1, %4;\n\tadd.u32 bl, %2, %4;\n\t"
       "mov.b64 ra, {al, %3};\n\tmov.b64 rb, {bl, %3};\n\t"
-      "setp.ne.b32 p, %6, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], ra, rb, %5, p;\n\t}" ::"r"(d_tmem),
+      "setp.ne.b32 p, %6, 0;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], ra, rb, %5, p;\n\t}" ::"r"(d_tmem),
       "r"(a_lo), "r"(b_lo), "r"(hi), "n"(OFF), "r"(idesc), "n"(ACC)
       : "memory");
 }
@@ -155,18 +160,20 @@ template <uint32_t ACOL, uint32_t BOFF>
 __device__ __forceinline__ void umma_ts_at(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t hi,
                                            uint32_t idesc, uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .b32 ra, bl;\n\t.reg .b64 rb;\n\t.reg .pred p;\n\t"
+      "{\n\t.reg .b32 ra, bl;\n\t.reg .b64 rb;\n\t.reg .pred p, e;\n\t"
       "add.u32 ra, %1, %4;\n\tadd.u32 bl, %2, %5;\n\tmov.b64 rb, {bl, %3};\n\t"
-      "setp.ne.b32 p, %7, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [ra], rb, %6, p;\n\t}" ::"r"(d_tmem),
+      "setp.ne.b32 p, %7, 0;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [ra], rb, %6, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "r"(b_lo), "r"(hi), "n"(ACOL), "n"(BOFF), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
-// Arrive on `bar` once every tcgen05 op issued so far by this thread has completed.
+// Arrive on `bar` once every tcgen05 op issued so far by the elected lane has completed.
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
-               : "memory");
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(bar)
+      : "memory");
 }
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
