@@ -231,6 +231,8 @@ def run_ours(args, cfg: AttnConfig):
     if world > 1:
         import datetime
 
+        # Keep rank 0's stdout to the one JSON line (NCCL prints its version at INFO/VERSION).
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
 
     def barrier():
