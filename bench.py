@@ -16,7 +16,9 @@ CUDA events on the launching stream, max over ranks.  Rank 0 prints one JSON lin
 `--impl reference` times the reference's own CPU attention
 (benchmark/cpp/correctness_v6.cu:23-72, built from its sources into oracle/_ref)
 on the host cores, one bounded sample of the same workload per step; it falls
-back to the restated oracle port if oracle/_ref was not built.
+back to the restated oracle port if oracle/_ref was not built.  With
+`--ref-device gpu` it times the reference's own CUDA kernel instead, on the
+workloads that kernel supports (fp16, d=128, non-causal: cfg4_d128, cfg2_f16nc).
 """
 from __future__ import annotations
 
@@ -56,6 +58,9 @@ def parse_args():
     ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ref-device", choices=["cpu", "gpu"], default="cpu",
+                    help="with --impl reference: gpu times the reference's own CUDA kernel instead "
+                         "(fp16, d=128, non-causal workloads only, e.g. cfg4_d128 or cfg2_f16nc)")
     return ap.parse_args()
 
 
@@ -155,10 +160,55 @@ def cpu_kind():
     return orc.ref_available(), ("reference" if orc.ref_available() else "port")
 
 
+def run_reference_gpu(args, cfg: AttnConfig):
+    """The reference's own GPU forward (flash_attention_forward_v6_mma, mma.sync,
+    through its pybind source compiled by oracle/build_ref_ext.py), timed like our
+    arm on one GPU: inputs resident in HBM, W warm-up steps, K steps between
+    synchronizes, CUDA events on the current stream."""
+    from oracle import oracle as orc
+
+    base = {"impl": "reference", "device": "gpu", "metric": METRIC, "unit": "TFLOPS", "higher_is_better": True,
+            "config": workload_config(cfg, 1, "weak"),
+            "kernel": "flash_attention_forward_v6_mma (src/forward/forward_v6_mma.cuh:325-412), mma.sync, sm_100"}
+    why = None
+    if cfg.dtype != torch.float16 or cfg.head_dim != 128 or cfg.causal or cfg.seq_len % 64:
+        why = "the reference GPU kernel supports fp16, d=128, non-causal, N % 64 == 0 only"
+    elif not torch.cuda.is_available():
+        why = "no CUDA device"
+    elif not orc.ref_gpu_available():
+        why = f"{orc.REF_EXT_SO} not built (python oracle/build_ref_ext.py)"
+    if why:
+        print(json.dumps({**base, "unavailable": why}), flush=True)
+        return
+    from flash_attention_runtime.inputs import generate
+
+    mod = orc.ref_gpu_module()
+    dev = torch.device("cuda", 0)
+    q, k, v = (x.to(dev) for x in generate(cfg))
+    o = torch.empty_like(q)
+    for _ in range(max(args.warmup, 3)):
+        mod.forward(q, k, v, o, False)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        mod.forward(q, k, v, o, False)
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / args.steps
+    value = cfg.flops() / (ms * 1e-3) / 1e12
+    print(json.dumps({**base, "value": value, "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3),
+                      "ms_per_step": ms, "dtype": "f16", "data": "synthetic",
+                      "l2": "inputs larger than L2 (126 MB); no flush needed"}), flush=True)
+
+
 def run_reference_arm(args, cfg: AttnConfig):
     rank, world, _ = dist_env()
     if rank != 0:
         return  # the reference CPU path does not shard; rank 0 alone runs it
+    if args.ref_device == "gpu":
+        run_reference_gpu(args, cfg)
+        return
     from oracle import oracle as orc
 
     use_ref, kind = cpu_kind()

@@ -68,6 +68,9 @@ CONFIGS = {
     "cfg4_d32": AttnConfig("cfg4_d32", 16, 16, 2048, 32, torch.float16, False, 4, outliers=True),
     "cfg4_d64": AttnConfig("cfg4_d64", 16, 16, 2048, 64, torch.float16, False, 4, outliers=True),
     "cfg4_d128": AttnConfig("cfg4_d128", 16, 16, 2048, 128, torch.float16, False, 4, outliers=True),
+    # fp16 non-causal companion of configuration 2: the largest of these shapes the
+    # reference's own GPU kernel supports (fp16, d = 128, non-causal, N % 64 == 0).
+    "cfg2_f16nc": AttnConfig("cfg2_f16nc", 8, 32, 4096, 128, torch.float16, False, 2),
 }
 
 

@@ -111,6 +111,30 @@ def ref_attention_direct(q, k, v, scale: float, causal: bool):
     return o
 
 
+REF_EXT_SO = HERE / "_ref" / "ext" / "fa_ref_v6.so"
+
+
+def ref_gpu_available() -> bool:
+    return REF_EXT_SO.exists()
+
+
+def ref_gpu_module():
+    """The reference's own pybind module (python/flash_attention_runtime/_ext.cu,
+    kernel flash_attention_forward_v6_mma), as built by oracle/build_ref_ext.py.
+    Its ``forward(q, k, v, o, benchmark)`` returns ``(o, ms)``; fp16, d = 128,
+    non-causal, N % 64 == 0 only."""
+    import importlib.util
+
+    import torch  # noqa: F401  (the module links against libtorch)
+
+    if not REF_EXT_SO.exists():
+        raise RuntimeError(f"{REF_EXT_SO} is missing: run `python oracle/build_ref_ext.py`")
+    spec = importlib.util.spec_from_file_location("fa_ref_v6", str(REF_EXT_SO))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
 def host_threads() -> int:
     try:
         return len(os.sched_getaffinity(0))
