@@ -120,6 +120,31 @@ __device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity, vola
   }
 }
 
+// Bounded wait for roles off the critical path (TMA producer, epilogue): the
+// hardware may suspend the waiting thread (up to 20 us per try, it resumes when
+// the phase completes), so it does not take issue slots from the softmax warps
+// on its SM sub-partition.
+__device__ __forceinline__ bool sleepy_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                            const KernelParams& p, int where) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > p.timeout_ns) {
+      *abort_flag = 1;
+      if (p.status) atomicCAS(p.status, 0, 0x100 | where);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ bool sleepy_warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                                 const KernelParams& p, int where) {
+  const bool ok = sleepy_wait(bar, parity, abort_flag, p, where);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // Warp-uniform bounded wait: every lane polls, the warp agrees on the outcome.
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                           const KernelParams& p, int where) {
@@ -287,7 +312,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       uint32_t kv_armed = 0, q_armed = 0, kv_par = 0, q_par = 0;
       bool ok = true;
       auto load_q = [&](int i, const TileInfo& t) -> bool {
-        if (!bounded_wait(bar(Q_EMPTY + i), (q_cnt[i] & 1) ^ 1, abort_flag, p, kWaitQEmpty)) return false;
+        if (!sleepy_wait(bar(Q_EMPTY + i), (q_cnt[i] & 1) ^ 1, abort_flag, p, kWaitQEmpty)) return false;
         const uint32_t fb = bar(Q_FULL + i);
         mbar_arrive_expect_tx(fb, C::TILE_BYTES);
         q_armed |= 1u << i;
@@ -305,7 +330,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       auto load_pair = [&](int v, int k, const TileInfo& t) -> bool {
         const uint32_t pr = kv_cnt % C::NPAIRS;
         const uint32_t ph = (kv_cnt / C::NPAIRS) & 1;
-        if (!bounded_wait(bar(KV_EMPTY + pr), ph ^ 1, abort_flag, p, kWaitKvEmpty)) return false;
+        if (!sleepy_wait(bar(KV_EMPTY + pr), ph ^ 1, abort_flag, p, kWaitKvEmpty)) return false;
         const uint32_t fb = bar(KV_FULL + pr);
         mbar_arrive_expect_tx(fb, (v >= 0 ? C::TILE_BYTES : 0u) + (k >= 0 ? C::TILE_BYTES : 0u));
         kv_armed |= 1u << pr;
@@ -327,7 +352,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       };
       while (ok) {
         const uint32_t slot = sched_cnt & 1;
-        if (!bounded_wait(bar(SCHED_EMPTY + slot), ((sched_cnt >> 1) & 1) ^ 1, abort_flag, p, kWaitSched)) break;
+        if (!sleepy_wait(bar(SCHED_EMPTY + slot), ((sched_cnt >> 1) & 1) ^ 1, abort_flag, p, kWaitSched)) break;
         sched_tile[slot] = tile;
         mbar_arrive(bar(SCHED_FULL + slot));
         ++sched_cnt;
@@ -459,7 +484,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     uint32_t sched_cnt = 0, o_cnt[2] = {0, 0}, st_cnt[2] = {0, 0};
     while (true) {
       const uint32_t slot = sched_cnt & 1;
-      if (!warp_wait(bar(SCHED_FULL + slot), (sched_cnt >> 1) & 1, abort_flag, p, kWaitSched)) break;
+      if (!sleepy_warp_wait(bar(SCHED_FULL + slot), (sched_cnt >> 1) & 1, abort_flag, p, kWaitSched)) break;
       const int tile = sched_tile[slot];
       mbar_arrive(bar(SCHED_EMPTY + slot));
       ++sched_cnt;
@@ -469,8 +494,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       for (int i = 0; i < 2 && !failed; ++i) {
         if ((i == 0 ? t.n0 : t.n1) == 0) continue;
         const uint32_t ss = st_cnt[i] & 1;
-        if (!warp_wait(bar(STATS_FULL + 2 * i + ss), (st_cnt[i] >> 1) & 1, abort_flag, p, kWaitStatsFull) ||
-            !warp_wait(bar(O_FULL + i), o_cnt[i] & 1, abort_flag, p, kWaitOFull)) {
+        if (!sleepy_warp_wait(bar(STATS_FULL + 2 * i + ss), (st_cnt[i] >> 1) & 1, abort_flag, p, kWaitStatsFull) ||
+            !sleepy_warp_wait(bar(O_FULL + i), o_cnt[i] & 1, abort_flag, p, kWaitOFull)) {
           failed = true;
           break;
         }
