@@ -281,9 +281,22 @@ def run_ours(args, cfg: AttnConfig):
     if world > 1:
         import datetime
 
-        # Keep rank 0's stdout to the one JSON line (NCCL prints its version at INFO/VERSION).
+        # Keep rank 0's stdout to the one JSON line: NCCL prints its version line on
+        # stdout when its communicator is created (at NCCL_DEBUG=VERSION or INFO,
+        # whatever the environment set), so the setup and a first barrier run with
+        # file descriptor 1 pointed at stderr.
         os.environ.setdefault("NCCL_DEBUG", "WARN")
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        sys.stdout.flush()
+        saved_stdout = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+            dist.barrier()
+            torch.cuda.synchronize(dev)
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved_stdout, 1)
+            os.close(saved_stdout)
 
     def barrier():
         if world > 1:
