@@ -200,7 +200,7 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 // polynomial fitted for this kernel by a Remez exchange for minimax relative
 // error on [-0.5, 0.5] (max relative error 2.6e-6); 2^n applied by adding n to
 // the exponent field.  x is clamped to >= -125 so the result stays a normal
-// number; callers use it only for finite x <= 2^8 (unmasked scores).
+// number (x = -inf, a masked score, gives 2^-125); callers pass x <= 2^8.
 __device__ __forceinline__ float2 exp2_fma(float2 x) {
   constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
   x.x = fmaxf(x.x, -125.0f);
@@ -579,16 +579,20 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 #pragma unroll
           for (int c = 0; c < kBlockN; ++c) s[c] = c > lim ? -INFINITY : s[c];
         }
-        // row max: 8 independent 3-input max chains, then a small tree
-        float mx[8];
+        // row max as a breadth-first tree of 3-input maxima (42 independent
+        // triples, then 14, 5 and 2), so the scheduler always has independent work
+        float m1[43];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          mx[k] = fmax3(s[16 * k], s[16 * k + 1], s[16 * k + 2]);
+        for (int k = 0; k < 42; ++k) m1[k] = fmax3(s[3 * k], s[3 * k + 1], s[3 * k + 2]);
+        m1[42] = fmaxf(s[126], s[127]);
+        float m2[15];
 #pragma unroll
-          for (int e = 3; e < 15; e += 2) mx[k] = fmax3(mx[k], s[16 * k + e], s[16 * k + e + 1]);
-          mx[k] = fmaxf(mx[k], s[16 * k + 15]);
-        }
-        const float mt = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
+        for (int k = 0; k < 14; ++k) m2[k] = fmax3(m1[3 * k], m1[3 * k + 1], m1[3 * k + 2]);
+        m2[14] = m1[42];
+        float m3[5];
+#pragma unroll
+        for (int k = 0; k < 5; ++k) m3[k] = fmax3(m2[3 * k], m2[3 * k + 1], m2[3 * k + 2]);
+        const float mt = fmax3(fmax3(m3[0], m3[1], m3[2]), m3[3], m3[4]);
         const float m_new = fmaxf(m_ref, mt);
         // Lazy rescale: keep the old reference max unless the row max grew by
         // more than 2^8 (then O and l are scaled by alpha, after P is written).
@@ -609,37 +613,27 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         const float2 scale2 = make_float2(sl2, sl2);
         const float2 neg_mc = make_float2(-mc, -mc);
         float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-        if (masked) {
+        // One loop for every block (one copy of this code in the instruction
+        // cache).  A masked score (-inf) gives x = -inf, which the FMA-pipe exp2
+        // clamps to 2^-125: P is 2^-125 there instead of 0 (0 once rounded to
+        // fp16), 2^125 times below the row's largest P (the element that set the
+        // reference max has P = 1), so it changes no fp32 sum it enters.
 #pragma unroll
-          for (int c = 0; c < kBlockN / 64; ++c) {
-            uint32_t pk[32];
+        for (int c = 0; c < kBlockN / 64; ++c) {
+          uint32_t pk[32];
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const float2 x = fma2(make_float2(s[c * 64 + 2 * e], s[c * 64 + 2 * e + 1]), scale2, neg_mc);
-              const float2 pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-              acc[e & 3] = add2(acc[e & 3], pp);
-              pk[e] = pack2<BF16>(pp.x, pp.y);
+          for (int e = 0; e < 32; ++e) {
+            const float2 x = fma2(make_float2(s[c * 64 + 2 * e], s[c * 64 + 2 * e + 1]), scale2, neg_mc);
+            float2 pp;
+            if ((e & 7) < FA_EXP2_FMA_PAIRS) {
+              pp = exp2_fma(x);
+            } else {
+              pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
             }
-            tmem_st32(s_addr + c * 32, pk);
+            acc[e & 3] = add2(acc[e & 3], pp);
+            pk[e] = pack2<BF16>(pp.x, pp.y);
           }
-        } else {
-#pragma unroll
-          for (int c = 0; c < kBlockN / 64; ++c) {
-            uint32_t pk[32];
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const float2 x = fma2(make_float2(s[c * 64 + 2 * e], s[c * 64 + 2 * e + 1]), scale2, neg_mc);
-              float2 pp;
-              if ((e & 7) < FA_EXP2_FMA_PAIRS) {
-                pp = exp2_fma(x);
-              } else {
-                pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-              }
-              acc[e & 3] = add2(acc[e & 3], pp);
-              pk[e] = pack2<BF16>(pp.x, pp.y);
-            }
-            tmem_st32(s_addr + c * 32, pk);
-          }
+          tmem_st32(s_addr + c * 32, pk);
         }
         const float2 a = add2(add2(acc[0], acc[1]), add2(acc[2], acc[3]));
         l += a.x + a.y;
