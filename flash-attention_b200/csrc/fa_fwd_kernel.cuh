@@ -11,12 +11,16 @@
 //    slice so the K/V of the slices in flight stay in L2);
 //  * warp 12 : TMA producer - Q0/Q1 once per tile, then K/V tiles through a
 //              ring of STAGES shared-memory slots used two at a time: slot pair
-//              {V_j, K_j+1} (K_0 alone at a tile's start, V_n-1 alone at its end)
-//              behind one full and one empty mbarrier, so the MMA thread acquires
-//              and releases once per key block;
+//              {V_j, K_j+1} behind one full and one empty mbarrier, so the MMA
+//              thread acquires and releases once per key block.  A tile's last V
+//              shares its pair with the next tile's K_0 (K_0 alone only for a
+//              CTA's first tile), and the next tile's Q is prefetched into L2 a
+//              tile ahead;
 //  * warp 13 : MMA issuer   - tcgen05.mma S_i = Q_i K_j^T (smem x smem -> TMEM)
 //              and O_i += P_i V_j (P from TMEM, V from smem, O in TMEM); the
-//              warp runs converged and elect.sync picks the issuing lane;
+//              warp runs converged and elect.sync picks the issuing lane.  It
+//              issues the next tile's S_i(0) inside the current tile's last key
+//              block, so the stream PV0, S0, PV1, S1 runs on across tiles;
 //  * warps 0-3 / 4-7 : softmax warpgroup i for query tile i, one thread per row
 //              (= TMEM lane): tcgen05.ld of the S row, mask, row max, exp2 with
 //              the scale folded in (part of them on the FMA pipe, see exp2_fma),
@@ -25,9 +29,10 @@
 //              grows by more than 2^8);
 //  * warps 8-11 : epilogue warpgroup - O_i from TMEM, 1/l normalise, O store and
 //              logsumexp, so the softmax warps go straight on to the next tile;
-//  * warps 14-15 idle.  setmaxnreg gives softmax 184 registers per thread, the
-//    epilogue 80 and the producer / MMA warpgroup 64 (2*128*184 + 128*80 +
-//    128*64 = 64K, the whole register file).
+//  * warps 14-15 idle.  setmaxnreg gives softmax 176 registers per thread, the
+//    epilogue 80 and the producer / MMA warpgroup 80 (2*128*176 + 128*80 +
+//    128*80 = 64K, the whole register file; every warp of a warpgroup must
+//    request the same count).
 //
 // TMEM (512 columns x 128 lanes of 32 bit): S0 [0,128) S1 [128,256)
 // O0 [256,256+D) O1 [256+D,256+2D); P_i aliases the first 64 columns of S_i.
@@ -41,6 +46,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cstdint>
+#include <type_traits>
 
 #include "ptx.cuh"
 #include "umma_layout.h"
@@ -301,7 +307,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
 
   if (warp >= kProducerWarp) {
-    setmaxnreg_dec<64>();
+    setmaxnreg_dec<80>();
     if (warp == kProducerWarp && lane == 0) {
       // ---------------------------------------------------------- TMA producer
       const uint64_t pol_kv = l2_policy_evict_last();
@@ -325,9 +331,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         ++q_cnt[i];
         return true;
       };
-      // Loads V rows [128 v, 128 v + 128) into the pair's first slot and K rows
-      // [128 k, 128 k + 128) into its second (v or k < 0: that slot stays unused).
-      auto load_pair = [&](int v, int k, const TileInfo& t) -> bool {
+      // Loads V rows [128 v, 128 v + 128) of unit tv into the pair's first slot and
+      // K rows [128 k, 128 k + 128) of unit tk into its second (v or k < 0: that
+      // slot stays unused).  A unit's last V shares its pair with the next unit's
+      // first K, so the MMA warp can start the next unit inside the last step.
+      auto load_pair = [&](int v, const TileInfo& tv, int k, const TileInfo& tk) -> bool {
         const uint32_t pr = kv_cnt % C::NPAIRS;
         const uint32_t ph = (kv_cnt / C::NPAIRS) & 1;
         if (!sleepy_wait(bar(KV_EMPTY + pr), ph ^ 1, abort_flag, p, kWaitKvEmpty)) return false;
@@ -339,31 +347,57 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         if (v >= 0) {
 #pragma unroll
           for (int c = 0; c < C::CHUNKS; ++c)
-            tma_load_4d(dst + c * kBlockN * C::SW, &tmV, fb, c * int(C::SW / 2), v * kBlockN, t.h, t.b, pol_kv);
+            tma_load_4d(dst + c * kBlockN * C::SW, &tmV, fb, c * int(C::SW / 2), v * kBlockN, tv.h, tv.b, pol_kv);
         }
         if (k >= 0) {
 #pragma unroll
           for (int c = 0; c < C::CHUNKS; ++c)
-            tma_load_4d(dst + C::TILE_BYTES + c * kBlockN * C::SW, &tmK, fb, c * int(C::SW / 2), k * kBlockN, t.h,
-                        t.b, pol_kv);
+            tma_load_4d(dst + C::TILE_BYTES + c * kBlockN * C::SW, &tmK, fb, c * int(C::SW / 2), k * kBlockN, tk.h,
+                        tk.b, pol_kv);
         }
         ++kv_cnt;
         return true;
       };
-      while (ok) {
+      // Hands a unit index (or an end marker >= num_tiles) to the other roles.
+      auto publish = [&](int unit) -> bool {
         const uint32_t slot = sched_cnt & 1;
-        if (!sleepy_wait(bar(SCHED_EMPTY + slot), ((sched_cnt >> 1) & 1) ^ 1, abort_flag, p, kWaitSched)) break;
-        sched_tile[slot] = tile;
+        if (!sleepy_wait(bar(SCHED_EMPTY + slot), ((sched_cnt >> 1) & 1) ^ 1, abort_flag, p, kWaitSched)) return false;
+        sched_tile[slot] = unit;
         mbar_arrive(bar(SCHED_FULL + slot));
         ++sched_cnt;
-        if (tile >= p.num_tiles) break;
-        const int next = atomicAdd(p.tile_counter, 1) + static_cast<int>(gridDim.x);
-        const TileInfo t = decode_tile<CAUSAL>(tile, p);
-        const int nmax = max(t.n0, t.n1);
-        ok = load_q(0, t) && load_pair(-1, 0, t);
+        return true;
+      };
+      ok = publish(tile);
+      if (ok && tile < p.num_tiles) {
+        TileInfo t = decode_tile<CAUSAL>(tile, p);
+        ok = load_q(0, t) && load_pair(-1, t, 0, t);
         if (ok && t.n1 > 0) ok = load_q(1, t);
-        for (int j = 0; ok && j < nmax; ++j) ok = load_pair(j, j + 1 < nmax ? j + 1 : -1, t);
-        tile = next;
+        while (ok) {
+          const int next = atomicAdd(p.tile_counter, 1) + static_cast<int>(gridDim.x);
+          const bool has_next = next < p.num_tiles;
+          TileInfo tn = t;
+          if (has_next) {
+            // The next unit's Q is read from HBM once: start it towards L2 now,
+            // a unit ahead of its load into shared memory.
+            tn = decode_tile<CAUSAL>(next, p);
+            for (int i = 0; i < (tn.n1 > 0 ? 2 : 1); ++i)
+#pragma unroll
+              for (int c = 0; c < C::CHUNKS; ++c)
+                tma_prefetch_l2_4d(&tmQ, c * int(C::SW / 2), tn.pair * 256 + i * 128, tn.h, tn.b);
+          }
+          const int nmax = max(t.n0, t.n1);
+          for (int j = 0; ok && j + 1 < nmax; ++j) ok = load_pair(j, t, j + 1, t);
+          if (!ok) break;
+          ok = publish(next);
+          if (!ok) break;
+          if (!has_next) {
+            ok = load_pair(nmax - 1, t, -1, t);
+            break;
+          }
+          ok = load_pair(nmax - 1, t, 0, tn) && load_q(0, tn);
+          if (ok && tn.n1 > 0) ok = load_q(1, tn);
+          t = tn;
+        }
       }
       if (*abort_flag) {
         // Let every copy this thread started land before the CTA exits.
@@ -417,38 +451,61 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         tc_fence_after();
         return true;
       };
-      while (ok) {
+      // Reads the next unit index from the scheduler ring (-1: the wait failed).
+      auto read_unit = [&]() -> int {
         const uint32_t slot = sched_cnt & 1;
-        if (!bounded_wait(bar(SCHED_FULL + slot), (sched_cnt >> 1) & 1, abort_flag, p, kWaitSched)) break;
-        const int tile = sched_tile[slot];
+        if (!bounded_wait(bar(SCHED_FULL + slot), (sched_cnt >> 1) & 1, abort_flag, p, kWaitSched)) return -1;
+        const int unit = sched_tile[slot];
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(SCHED_EMPTY + slot));
         ++sched_cnt;
-        if (tile >= p.num_tiles) break;
+        return unit;
+      };
+      // S_i(0) of a unit with n_i key blocks for tile i, from the K tile in slot
+      // kslot (Q_i must land first).  I is a compile-time tile index.
+      auto issue_first_s = [&](auto I, int n_i, uint32_t kslot) -> bool {
+        constexpr int i = decltype(I)::value;
+        if (!bounded_wait(bar(Q_FULL + i), qf_cnt[i] & 1, abort_flag, p, kWaitQFull)) return false;
+        ++qf_cnt[i];
+        tc_fence_after();
+        issue_s(i, kslot);
+        umma_commit(bar(S_FULL + i));
+        if (n_i == 1) umma_commit(bar(Q_EMPTY + i));
+        return true;
+      };
+      int tile = read_unit();
+      ok = tile >= 0;
+      bool started = false;  // S_i(0) of this unit already issued in the previous unit's last step
+      while (ok && tile < p.num_tiles) {
         const TileInfo t = decode_tile<CAUSAL>(tile, p);
         const int n0 = t.n0, n1 = t.n1, nmax = max(n0, n1);
-        uint32_t pk;
-        ok = acquire(pk) && bounded_wait(bar(Q_FULL + 0), qf_cnt[0] & 1, abort_flag, p, kWaitQFull);
-        if (!ok) break;
-        ++qf_cnt[0];
-        tc_fence_after();
-        issue_s(0, 2 * pk + 1);
-        umma_commit(bar(S_FULL + 0));
-        if (n0 == 1) umma_commit(bar(Q_EMPTY + 0));
-        if (n1 > 0) {
-          if (!bounded_wait(bar(Q_FULL + 1), qf_cnt[1] & 1, abort_flag, p, kWaitQFull)) break;
-          ++qf_cnt[1];
-          tc_fence_after();
-          issue_s(1, 2 * pk + 1);
-          umma_commit(bar(S_FULL + 1));
-          if (n1 == 1) umma_commit(bar(Q_EMPTY + 1));
+        if (!started) {
+          uint32_t pk;
+          ok = acquire(pk) && issue_first_s(std::integral_constant<int, 0>{}, n0, 2 * pk + 1) &&
+               (n1 == 0 || issue_first_s(std::integral_constant<int, 1>{}, n1, 2 * pk + 1));
+          if (!ok) break;
+          umma_commit(bar(KV_EMPTY + pk));
         }
-        umma_commit(bar(KV_EMPTY + pk));
+        int next = p.num_tiles, next_n0 = 0, next_n1 = 0;
+        bool chain = false;
         for (int j = 0; j < nmax; ++j) {
           uint32_t pj;
           if (!acquire(pj)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sv = 2 * pj, skn = 2 * pj + 1;
+          const bool last = j == nmax - 1;
+          if (last) {
+            // The producer publishes the next unit before loading this pair, whose
+            // K slot holds that unit's first K tile.
+            next = read_unit();
+            if (next < 0) { ok = false; break; }
+            chain = next < p.num_tiles;
+            if (chain) {
+              const TileInfo tn = decode_tile<CAUSAL>(next, p);
+              next_n0 = tn.n0;
+              next_n1 = tn.n1;
+            }
+          }
           if (j < n0) {
             if (!wait_p(0, j)) { ok = false; break; }
             issue_pv(0, sv, j > 0);
@@ -458,6 +515,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             issue_s(0, skn);
             umma_commit(bar(S_FULL + 0));
             if (j + 2 == n0) umma_commit(bar(Q_EMPTY + 0));
+          } else if (last && chain) {
+            if (!issue_first_s(std::integral_constant<int, 0>{}, next_n0, skn)) { ok = false; break; }
           }
           if (j < n1) {
             if (!wait_p(1, j)) { ok = false; break; }
@@ -468,9 +527,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             issue_s(1, skn);
             umma_commit(bar(S_FULL + 1));
             if (j + 2 == n1) umma_commit(bar(Q_EMPTY + 1));
+          } else if (last && chain && next_n1 > 0) {
+            if (!issue_first_s(std::integral_constant<int, 1>{}, next_n1, skn)) { ok = false; break; }
           }
           umma_commit(bar(KV_EMPTY + pj));
         }
+        if (!ok) break;
+        tile = next;
+        started = true;
       }
       // Every MMA issued by this thread completes before TMEM and smem go away.
       umma_commit(bar(DRAIN));
@@ -536,7 +600,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     }
     tc_fence_before();
   } else {
-    setmaxnreg_inc<184>();
+    setmaxnreg_inc<176>();
     // ------------------------------------------------------------ softmax warpgroups
     const int wg = warp / 4;                    // query tile 0 or 1
     const int row_in_tile = threadIdx.x % 128;  // = TMEM lane
