@@ -14,8 +14,7 @@
 //              {V_j, K_j+1} behind one full and one empty mbarrier, so the MMA
 //              thread acquires and releases once per key block.  A tile's last V
 //              shares its pair with the next tile's K_0 (K_0 alone only for a
-//              CTA's first tile), and the next tile's Q is prefetched into L2 a
-//              tile ahead;
+//              CTA's first tile);
 //  * warp 13 : MMA issuer   - tcgen05.mma S_i = Q_i K_j^T (smem x smem -> TMEM)
 //              and O_i += P_i V_j (P from TMEM, V from smem, O in TMEM); the
 //              warp runs converged and elect.sync picks the issuing lane.  It
@@ -376,15 +375,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           const int next = atomicAdd(p.tile_counter, 1) + static_cast<int>(gridDim.x);
           const bool has_next = next < p.num_tiles;
           TileInfo tn = t;
-          if (has_next) {
-            // The next unit's Q is read from HBM once: start it towards L2 now,
-            // a unit ahead of its load into shared memory.
-            tn = decode_tile<CAUSAL>(next, p);
-            for (int i = 0; i < (tn.n1 > 0 ? 2 : 1); ++i)
-#pragma unroll
-              for (int c = 0; c < C::CHUNKS; ++c)
-                tma_prefetch_l2_4d(&tmQ, c * int(C::SW / 2), tn.pair * 256 + i * 128, tn.h, tn.b);
-          }
+          if (has_next) tn = decode_tile<CAUSAL>(next, p);
           const int nmax = max(t.n0, t.n1);
           for (int j = 0; ok && j + 1 < nmax; ++j) ok = load_pair(j, t, j + 1, t);
           if (!ok) break;
