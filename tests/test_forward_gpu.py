@@ -78,6 +78,18 @@ def test_ragged_seq_len(n, causal):
     _run_and_check(q, k, v, causal)
 
 
+@pytest.mark.parametrize("n,d", [(100, 64), (129, 128), (300, 32), (300, 128), (1000, 64)])
+@pytest.mark.parametrize("causal", [False, True])
+def test_ragged_many_units(n, d, causal):
+    """200 (b,h) slices, more work units than the 148 persistent CTAs, so each CTA
+    runs several units back to back (the next unit's first S is issued inside the
+    last key block of the current one), including units whose second 128-row query
+    tile lies past the sequence end (n = 100, 300).  Every slice is checked."""
+    dtype = torch.float16 if causal else torch.bfloat16
+    q, k, v = make_random((2, 100, n, d), dtype, seed=31 + n + d)
+    _run_and_check(q, k, v, causal)
+
+
 @pytest.mark.parametrize("d", [32, 64, 128])
 def test_cfg4_outliers_small(d):
     """Config-4 style large-logit outliers (1% of Q/K entries x20), smaller batch."""
