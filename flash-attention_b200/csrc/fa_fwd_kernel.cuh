@@ -48,6 +48,7 @@
 #include <type_traits>
 
 #include "ptx.cuh"
+#include "schedule.h"
 #include "umma_layout.h"
 
 #ifndef FA_EXP2_FMA_PAIRS
@@ -165,27 +166,9 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, uint64
   }
 }
 
-struct TileInfo {
-  int b, h, pair, n0, n1;
-};
-
 template <bool CAUSAL>
 __device__ __forceinline__ TileInfo decode_tile(int tile, const KernelParams& p) {
-  const int bh_total = p.batch * p.heads;
-  const int per_group = p.group_bh * p.n_pairs;
-  const int g = tile / per_group;
-  const int r = tile - g * per_group;
-  const int gsize = min(p.group_bh, bh_total - g * p.group_bh);
-  const int rank = r / gsize;
-  const int bh = g * p.group_bh + (r - rank * gsize);
-  TileInfo t;
-  t.b = bh / p.heads;
-  t.h = bh - t.b * p.heads;
-  t.pair = CAUSAL ? (p.n_pairs - 1 - rank) : rank;
-  const int q1 = t.pair * 256 + 128;
-  t.n0 = CAUSAL ? min(2 * t.pair + 1, p.n_kv) : p.n_kv;
-  t.n1 = q1 >= p.seq_len ? 0 : (CAUSAL ? min(2 * t.pair + 2, p.n_kv) : p.n_kv);
-  return t;
+  return decode_unit(tile, p.batch, p.heads, p.seq_len, p.n_pairs, p.n_kv, p.group_bh, kBlockN, CAUSAL);
 }
 
 template <bool BF16>

@@ -222,21 +222,18 @@ int fa_fwd_sm100(const fa_fwd_params* p, void* stream_ptr) {
   kp.heads = h;
   kp.seq_len = n;
   kp.scale_log2 = p->softmax_scale * 1.4426950408889634f;
-  kp.n_pairs = (n + 255) / 256;
-  kp.n_kv = (n + 127) / 128;
-  const long long tiles = static_cast<long long>(b) * h * kp.n_pairs;
-  if (tiles > (1ll << 30)) return fail(FA_ERR_BAD_SHAPE, "batch*heads*ceil(N/256) = %lld tiles is too many", tiles);
-  kp.num_tiles = static_cast<int>(tiles);
-  // Slices per scheduling group: about one wave of tiles, so the K/V of the
-  // slices in flight stay L2-resident while the heavy (causal) tiles go first.
-  int g = (di.sms + kp.n_pairs - 1) / kp.n_pairs;
-  if (g < 1) g = 1;
-  if (g > b * h) g = b * h;
-  kp.group_bh = g;
+  const fa::SchedPlan plan = fa::plan_schedule(b, h, n, fa::kBlockN, di.sms);
+  if (plan.num_tiles < 0)
+    return fail(FA_ERR_BAD_SHAPE, "batch*heads*ceil(N/256) = %lld tiles is too many",
+                static_cast<long long>(b) * h * plan.n_pairs);
+  kp.n_pairs = plan.n_pairs;
+  kp.n_kv = plan.n_kv;
+  kp.num_tiles = plan.num_tiles;
+  kp.group_bh = plan.group_bh;
   kp.tile_counter = static_cast<int*>(ws);
   kp.status = p->status;
   kp.timeout_ns = p->timeout_ns ? p->timeout_ns : 2000000000ull;
-  s.grid = static_cast<int>(tiles < di.sms ? tiles : di.sms);
+  s.grid = plan.grid;
   s.stream = stream;
   s.bf16 = bf16;
   s.causal = p->causal != 0;

@@ -1,0 +1,72 @@
+// Work units and their order.
+//
+// A work unit is a pair of 128-row query tiles (rows [256 p, 256 p + 256)) of one
+// (batch, head) slice.  The reference launches one CTA per 64-row query tile,
+// grid (N/64, H, B) (src/forward/forward_v6_mma.cuh:325-412); here persistent CTAs
+// take units from an atomic counter in that order:
+//  * slices are grouped, about one wave of units per group, so the K/V of the
+//    slices in flight stay in L2;
+//  * within a group, units go pair-major: for causal attention the pair with the
+//    most key blocks (the last one) first, so the lightest units end the launch.
+//
+// Plain integer arithmetic, shared by the host (planning, unit tests) and the
+// kernel (decoding).
+#pragma once
+
+#include "umma_layout.h"  // FA_HD
+
+namespace fa {
+
+constexpr int kUnitRows = 256;  // query rows per work unit (two 128-row tiles)
+
+struct SchedPlan {
+  int n_pairs;    // ceil(N / 256): units per slice
+  int n_kv;       // ceil(N / key_block): key/value blocks per slice
+  int num_tiles;  // batch * heads * n_pairs
+  int group_bh;   // slices per scheduling group
+  int grid;       // persistent CTAs: min(num_tiles, sms)
+};
+
+// Host plan for B x H slices of N rows on a GPU with `sms` SMs.
+FA_HD SchedPlan plan_schedule(int batch, int heads, int seq_len, int key_block, int sms) {
+  SchedPlan s;
+  s.n_pairs = (seq_len + kUnitRows - 1) / kUnitRows;
+  s.n_kv = (seq_len + key_block - 1) / key_block;
+  const long long tiles = static_cast<long long>(batch) * heads * s.n_pairs;
+  s.num_tiles = tiles > (1ll << 30) ? -1 : static_cast<int>(tiles);  // -1: too many
+  int g = (sms + s.n_pairs - 1) / s.n_pairs;
+  if (g < 1) g = 1;
+  if (g > batch * heads) g = batch * heads;
+  s.group_bh = g;
+  s.grid = static_cast<int>(tiles < sms ? tiles : sms);
+  return s;
+}
+
+struct TileInfo {
+  int b, h, pair, n0, n1;  // slice, unit, key blocks of query tile 0 and 1 (0: tile past N)
+};
+
+// Unit index -> slice, pair and key-block counts.
+FA_HD TileInfo decode_unit(int tile, int batch, int heads, int seq_len, int n_pairs, int n_kv, int group_bh,
+                           int key_block, bool causal) {
+  const int bh_total = batch * heads;
+  const int per_group = group_bh * n_pairs;
+  const int g = tile / per_group;
+  const int r = tile - g * per_group;
+  const int gsize = (group_bh < bh_total - g * group_bh) ? group_bh : bh_total - g * group_bh;
+  const int rank = r / gsize;
+  const int bh = g * group_bh + (r - rank * gsize);
+  TileInfo t;
+  t.b = bh / heads;
+  t.h = bh - t.b * heads;
+  t.pair = causal ? (n_pairs - 1 - rank) : rank;
+  const int q1 = t.pair * kUnitRows + 128;
+  // causal: key blocks up to the one holding the tile's last row
+  const int c0 = (t.pair * kUnitRows + 128 + key_block - 1) / key_block;
+  const int c1 = (t.pair * kUnitRows + 256 + key_block - 1) / key_block;
+  t.n0 = causal ? (c0 < n_kv ? c0 : n_kv) : n_kv;
+  t.n1 = q1 >= seq_len ? 0 : (causal ? (c1 < n_kv ? c1 : n_kv) : n_kv);
+  return t;
+}
+
+}  // namespace fa
