@@ -145,6 +145,33 @@ __device__ __forceinline__ bool sleepy_wait(uint32_t bar, uint32_t parity, volat
   }
 }
 
+// Wait of the softmax warps for their next S tile.  It polls once; then the
+// hardware may suspend the warp for up to kSoftmaxSleepNs per try, so that a
+// waiting softmax warp does not take issue slots from the other warpgroup's
+// softmax warp on the same SM sub-partition.  The bound keeps the wake-up late
+// by at most that much.
+constexpr uint32_t kSoftmaxSleepNs = 200;
+__device__ __forceinline__ bool short_sleep_warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                                      const KernelParams& p, int where) {
+  bool ok = mbar_try_wait(bar, parity);
+  if (!ok) {
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+      if (mbar_try_wait_sleep(bar, parity, kSoftmaxSleepNs)) {
+        ok = true;
+        break;
+      }
+      if (*abort_flag) break;
+      if (globaltimer_ns() - t0 > p.timeout_ns) {
+        *abort_flag = 1;
+        if (p.status) atomicCAS(p.status, 0, 0x100 | where);
+        break;
+      }
+    }
+  }
+  return __all_sync(0xffffffffu, ok);
+}
+
 __device__ __forceinline__ bool sleepy_warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                                  const KernelParams& p, int where) {
   const bool ok = sleepy_wait(bar, parity, abort_flag, p, where);
@@ -597,7 +624,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       float m_ref = -INFINITY, l = 0.f;
       bool failed = false;
       for (int j = 0; j < n; ++j) {
-        if (!warp_wait(bar(S_FULL + wg), s_cnt & 1, abort_flag, p, kWaitSFull)) { failed = true; break; }
+        if (!short_sleep_warp_wait(bar(S_FULL + wg), s_cnt & 1, abort_flag, p, kWaitSFull)) { failed = true; break; }
         ++s_cnt;
         tc_fence_after();
         float s[kBlockN];
