@@ -214,13 +214,13 @@ def run_reference_arm(args, cfg: AttnConfig):
     use_ref, kind = cpu_kind()
     threads = orc.host_threads()
     n_slices = threads  # one slice per host thread per step
-    # A step takes seconds on the CPU: run at most one warm-up step, and only as
-    # many timed steps as fit in REF_BUDGET_S (the line reports the steps run).
-    warm = min(args.warmup, 1)
+    # A step takes seconds on the CPU: run at most three warm-up steps, and only
+    # as many timed steps as fit in REF_BUDGET_S (the line reports the steps run).
+    warm = min(args.warmup, 3)
     times = []
     for _ in range(warm):
         times.append(cpu_sample(cfg, n_slices, threads, use_ref))
-    est = times[0] if times else None
+    est = float(np.median(times)) if times else None
     steps = args.steps if est is None else max(1, min(args.steps, int(REF_BUDGET_S / max(est, 1e-3))))
     times = [cpu_sample(cfg, n_slices, threads, use_ref) for _ in range(steps)]
     t = float(np.mean(times))
