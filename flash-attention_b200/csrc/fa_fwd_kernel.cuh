@@ -233,28 +233,70 @@ __device__ __forceinline__ float2 exp2_fma(float2 x) {
   return r;
 }
 
-// S_i = Q_i K^T: D/16 MMAs of K = 16.  Step kk reads bytes kk*32 of each
-// swizzled row, in column chunk (kk*32)/SW (chunks are 128*SW bytes apart).
-template <int D, int KK = 0>
+// S_i = Q_i K^T: D/16 MMAs of K = 16 in one asm block with one elect.sync, so
+// the issuing warp takes few issue slots from the softmax warps on its SM
+// sub-partition.  Step kk adds ((kk*32)/SW)*(128*SW/16) + ((kk*32)%SW)/16 to the
+// low word of both descriptors (16-byte units; no carry, shared memory offsets
+// stay below 2^18 bytes).
+#define FA_SS2(off, pred)                                                   \
+  "add.u32 al, %1, " #off ";\n\tadd.u32 bl, %2, " #off ";\n\t"              \
+  "mov.b64 ra, {al, %3};\n\tmov.b64 rb, {bl, %3};\n\t"                     \
+  "@e tcgen05.mma.cta_group::1.kind::f16 [%0], ra, rb, %4, " #pred ";\n\t"
+#define FA_SS2_HEAD                                                         \
+  "{\n\t.reg .b32 al, bl;\n\t.reg .b64 ra, rb;\n\t.reg .pred e, pf, pt;\n\t" \
+  "setp.ne.b32 pf, %4, %4;\n\tsetp.eq.b32 pt, %4, %4;\n\t"                 \
+  "elect.sync _|e, 0xffffffff;\n\t"
+template <int D>
 __device__ __forceinline__ void mma_chain_s(uint32_t d, uint32_t a_lo, uint32_t b_lo, uint32_t hi, uint32_t idesc) {
-  if constexpr (KK < D / 16) {
-    constexpr uint32_t sw = Cfg<D>::SW;
-    constexpr uint32_t off = ((KK * 32u) / sw) * (kBlockM * sw / 16) + ((KK * 32u) % sw) / 16;
-    umma_ss_at<off, KK == 0 ? 0u : 1u>(d, a_lo, b_lo, hi, idesc);
-    mma_chain_s<D, KK + 1>(d, a_lo, b_lo, hi, idesc);
+  if constexpr (D == 128) {
+    static_assert(Cfg<D>::SW == 128, "layout");
+    asm volatile(FA_SS2_HEAD FA_SS2(0, pf) FA_SS2(2, pt) FA_SS2(4, pt) FA_SS2(6, pt) FA_SS2(1024, pt)
+                     FA_SS2(1026, pt) FA_SS2(1028, pt) FA_SS2(1030, pt) "}" ::"r"(d),
+                 "r"(a_lo), "r"(b_lo), "r"(hi), "r"(idesc)
+                 : "memory");
+  } else if constexpr (D == 64) {
+    static_assert(Cfg<D>::SW == 128, "layout");
+    asm volatile(FA_SS2_HEAD FA_SS2(0, pf) FA_SS2(2, pt) FA_SS2(4, pt) FA_SS2(6, pt) "}" ::"r"(d), "r"(a_lo),
+                 "r"(b_lo), "r"(hi), "r"(idesc)
+                 : "memory");
+  } else {
+    static_assert(Cfg<D>::SW == 64, "layout");
+    asm volatile(FA_SS2_HEAD FA_SS2(0, pf) FA_SS2(2, pt) "}" ::"r"(d), "r"(a_lo), "r"(b_lo), "r"(hi), "r"(idesc)
+                 : "memory");
   }
 }
+#undef FA_SS2_HEAD
+#undef FA_SS2
 
-// O_i += P_i V: 8 MMAs of K = 16 rows of V; P step kk is TMEM columns
-// [8kk, 8kk+8) of the S_i region (16 16-bit values packed two per column).
-template <int D, int KK = 0>
+// O_i += P_i V: 8 MMAs of K = 16 rows of V in one asm block; P step kk is TMEM
+// columns [8kk, 8kk+8) of the S_i region, V step kk starts SW 16-byte units on.
+#define FA_TS2(acol, boff, pred)                                            \
+  "add.u32 ra, %1, " #acol ";\n\tadd.u32 bl, %2, " #boff ";\n\t"            \
+  "mov.b64 rb, {bl, %3};\n\t"                                              \
+  "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [ra], rb, %4, " #pred ";\n\t"
+#define FA_TS2_HEAD                                                         \
+  "{\n\t.reg .b32 ra, bl;\n\t.reg .b64 rb;\n\t.reg .pred e, pa, pt;\n\t"    \
+  "setp.ne.b32 pa, %5, 0;\n\tsetp.eq.b32 pt, %4, %4;\n\t"                  \
+  "elect.sync _|e, 0xffffffff;\n\t"
+template <int D>
 __device__ __forceinline__ void mma_chain_pv(uint32_t d, uint32_t a, uint32_t b_lo, uint32_t hi, uint32_t idesc,
                                              uint32_t acc) {
-  if constexpr (KK < kBlockN / 16) {
-    umma_ts_at<KK * 8u, KK * 16u * Cfg<D>::SW / 16>(d, a, b_lo, hi, idesc, KK == 0 ? acc : 1u);
-    mma_chain_pv<D, KK + 1>(d, a, b_lo, hi, idesc, acc);
+  static_assert(kBlockN == 128, "8 steps of 16 keys");
+  if constexpr (Cfg<D>::SW == 128) {
+    asm volatile(FA_TS2_HEAD FA_TS2(0, 0, pa) FA_TS2(8, 128, pt) FA_TS2(16, 256, pt) FA_TS2(24, 384, pt)
+                     FA_TS2(32, 512, pt) FA_TS2(40, 640, pt) FA_TS2(48, 768, pt) FA_TS2(56, 896, pt) "}" ::"r"(d),
+                 "r"(a), "r"(b_lo), "r"(hi), "r"(idesc), "r"(acc)
+                 : "memory");
+  } else {
+    static_assert(Cfg<D>::SW == 64, "layout");
+    asm volatile(FA_TS2_HEAD FA_TS2(0, 0, pa) FA_TS2(8, 64, pt) FA_TS2(16, 128, pt) FA_TS2(24, 192, pt)
+                     FA_TS2(32, 256, pt) FA_TS2(40, 320, pt) FA_TS2(48, 384, pt) FA_TS2(56, 448, pt) "}" ::"r"(d),
+                 "r"(a), "r"(b_lo), "r"(hi), "r"(idesc), "r"(acc)
+                 : "memory");
   }
 }
+#undef FA_TS2_HEAD
+#undef FA_TS2
 
 template <int D, bool BF16, bool CAUSAL>
 __global__ void __launch_bounds__(kNumThreads, 1)
@@ -409,7 +451,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }
     } else if (warp == kMmaWarp) {
       // ---------------------------------------------------------- MMA issuer
-      // All 32 lanes run this loop (see the elect.sync wrappers in ptx.cuh).  A
+      // All 32 lanes run this loop (elect.sync in the MMA chains and commits).  A
       // wait's try_wait is one instruction for the whole warp, so every lane sees
       // the same outcome and the loop stays converged; single arrivals come from
       // lane 0.

@@ -123,64 +123,12 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// D[tmem] (+)= A[smem desc] * B[smem desc]; 16-bit inputs, fp32 accumulate.
-__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                        uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// D[tmem] (+)= A[tmem] * B[smem desc]; A is read from tensor memory.
-__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                        uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// The MMA warp runs converged: every lane executes the loop (so descriptors and
+// The MMA warp runs converged: every lane executes its loop (so descriptors and
 // addresses are warp-uniform and stay on the uniform datapath) and each tcgen05
-// instruction below is issued by the lane elect.sync picks.  With the full mask
-// that is always the lowest lane, so all MMAs and commits come from one thread,
-// as tcgen05.commit's completion tracking requires.
-
-// One tcgen05.mma (kind::f16, A and B from smem descriptors).  A descriptor is
-// passed as its low word (start address | leading byte offset) and its high word
-// (stride byte offset | version | layout); step OFF of a chain adds OFF to the
-// start address (16-byte units) of both.  The low-word add cannot carry: shared
-// memory addresses stay below 2^18 bytes.
-template <uint32_t OFF, uint32_t ACC>
-__device__ __forceinline__ void umma_ss_at(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t hi,
-                                           uint32_t idesc) {
-  asm volatile(
-      "{\n\t.reg .b32 al, bl;\n\t.reg .b64 ra, rb;\n\t.reg .pred p, e;\n\t"
-      "add.u32 al, %1, %4;\n\tadd.u32 bl, %2, %4;\n\t"
-      "mov.b64 ra, {al, %3};\n\tmov.b64 rb, {bl, %3};\n\t"
-      "setp.ne.b32 p, %6, 0;\n\telect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], ra, rb, %5, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_lo), "r"(b_lo), "r"(hi), "n"(OFF), "r"(idesc), "n"(ACC)
-      : "memory");
-}
-
-// One tcgen05.mma with A from TMEM column a_tmem + ACOL and B = (b_lo + BOFF, hi).
-template <uint32_t ACOL, uint32_t BOFF>
-__device__ __forceinline__ void umma_ts_at(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t hi,
-                                           uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .b32 ra, bl;\n\t.reg .b64 rb;\n\t.reg .pred p, e;\n\t"
-      "add.u32 ra, %1, %4;\n\tadd.u32 bl, %2, %5;\n\tmov.b64 rb, {bl, %3};\n\t"
-      "setp.ne.b32 p, %7, 0;\n\telect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [ra], rb, %6, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "r"(b_lo), "r"(hi), "n"(ACOL), "n"(BOFF), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
+// instruction is issued by the lane elect.sync picks.  With the full mask that is
+// always the lowest lane, so all MMAs and commits come from one thread, as
+// tcgen05.commit's completion tracking requires.  The MMA chains themselves are
+// written out in fa_fwd_kernel.cuh (one asm block and one elect.sync per chain).
 
 // Arrive on `bar` once every tcgen05 op issued so far by the elected lane has completed.
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
@@ -273,11 +221,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-// Named barrier over `nthreads` threads (a multiple of 32).
-__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 __device__ __forceinline__ void st_global_v4(void* ptr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
