@@ -140,6 +140,42 @@ def test_strided_bnhd_layout():
     assert compare_lse(lse, ref_lse)["ok"]
 
 
+@pytest.mark.parametrize("big_dim", [0, 1])
+def test_strides_past_2_31_elements(big_dim):
+    """A batch (big_dim=0) or head (big_dim=1) stride of 2^31 + 1024 elements, which
+    only the 64-bit stride fields of fa_fwd_params can carry.  Q, K, V and O are
+    views at different offsets into one 4.3 GB buffer, each touching two 32K-element
+    islands 2^31 + 1024 elements apart; nothing else of the buffer is read."""
+    shape = (2, 2, 256, 64) if big_dim == 0 else (1, 2, 256, 64)
+    b, h, n, d = shape
+    big = (1 << 31) + 1024
+    inner = h * n * d if big_dim == 0 else n * d  # span below the big stride
+    strides = (big, n * d, d, 1) if big_dim == 0 else (h * big, big, d, 1)
+    dev = torch.device("cuda", 0)
+    buf = torch.empty(big + 4 * inner, dtype=torch.bfloat16, device=dev)
+    views = [buf.as_strided(shape, strides, storage_offset=i * inner) for i in range(4)]
+    q, k, v = make_random(shape, torch.bfloat16, seed=31 + big_dim)
+    for dst, src in zip(views, (q, k, v)):
+        dst.copy_(src.to(dev))
+    out = views[3]
+    out.fill_(float("nan"))
+    assert max(t.stride(big_dim) for t in views) > 2 ** 31
+    lse = torch.empty((b, h, n), dtype=torch.float32, device=dev)
+    ret, _ = fa.ext_forward(views[0], views[1], views[2], out, False, 0.125, True, lse)
+    assert ret.data_ptr() == out.data_ptr()
+    torch.cuda.synchronize(dev)
+    ref_o, ref_lse = oracle_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), 0.125, True)
+    ro = compare_output(out, ref_o, torch.bfloat16)
+    rl = compare_lse(lse, ref_lse)
+    assert ro["ok"], ro
+    assert rl["ok"], rl
+    # the inputs were not overwritten
+    for view, src in zip(views, (q, k, v)):
+        assert torch.equal(view.cpu(), src)
+    del views, out, buf
+    torch.cuda.empty_cache()
+
+
 def test_forward_timed_and_reference_call_shape():
     """forward(q,k,v) with the reference defaults, forward_timed returns (o, ms)."""
     q, k, v = make_random((1, 2, 256, 128), torch.float16, seed=5)
