@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include "fa_fwd_kernel.cuh"
+#include "fa_sm100.h"
 
 namespace fa {
 
@@ -20,6 +21,9 @@ struct LaunchSpec {
 
 // Sets the message fa_last_error() returns on this host thread.
 void set_last_error(const char* msg);
+// fa_fwd_sm100's device-free argument checks alone (status code, message in
+// fa_last_error()).
+int validate_params(const fa_fwd_params* p);
 
 cudaError_t launch_d32(const LaunchSpec& s);
 cudaError_t launch_d64(const LaunchSpec& s);

@@ -62,7 +62,10 @@ int scratch_address(int dev, void** out) {
 extern "C" {
 
 int fa_fwd_sm100_noalloc(const fa_fwd_params* p, void* stream) {
-  if (p == nullptr) return fa_fwd_sm100(nullptr, stream);  // reports FA_ERR_BAD_PARAM
+  // The argument checks come first, as in fa_fwd_sm100: a bad call is rejected
+  // before any CUDA runtime call.
+  const int vrc = fa::validate_params(p);
+  if (vrc != FA_OK) return vrc;
   if (p->workspace != nullptr) {
     fa::set_last_error("fa_fwd_sm100_noalloc: params->workspace must be NULL (this entry point uses its own static scratch)");
     return FA_ERR_BAD_PARAM;

@@ -91,12 +91,19 @@ void* default_workspace(int dev, cudaStream_t stream) {
 
 int64_t pick(int64_t wide, int narrow) { return wide != 0 ? wide : static_cast<int64_t>(narrow); }
 
+// Largest stride, in elements, that a TMA tensor map takes: strides are below 2^40 bytes.
+constexpr int64_t kMaxStride = int64_t(1) << 39;
+// Largest extent of a tensor, in elements (2^48 bytes, above any device memory);
+// it keeps the kernel's 64-bit O and LSE addressing far from overflow.
+constexpr int64_t kMaxExtent = int64_t(1) << 47;
+
 int encode_map(CUtensorMap* map, void* base, int d, int n, int h, int b, int64_t s_seq, int64_t s_head,
                int64_t s_batch, bool bf16, const char* name) {
   const uint32_t sw = fa::swizzle_bytes(d);
-  // A stride of a size-1 dimension is never followed; give TMA a valid one.
-  if (h == 1) s_head = s_seq * n;
-  if (b == 1) s_batch = s_head * h;
+  // A stride of a size-1 dimension is never followed; give TMA a valid one (a
+  // multiple of 16 bytes below 2^40 bytes).
+  if (h == 1) s_head = s_seq * n < kMaxStride ? s_seq * n : s_seq;
+  if (b == 1) s_batch = s_head * h < kMaxStride ? s_head * h : s_head;
   cuuint64_t dims[4] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(h),
                         static_cast<cuuint64_t>(b)};
   cuuint64_t strides[3] = {static_cast<cuuint64_t>(s_seq) * 2, static_cast<cuuint64_t>(s_head) * 2,
@@ -115,10 +122,68 @@ int encode_map(CUtensorMap* map, void* base, int d, int n, int h, int b, int64_t
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+struct Strides {
+  int64_t seq[4], head[4], batch[4];  // elements; index 0..3 = Q, K, V, O
+};
+
+// Every check that needs no device, in a fixed order; the first failure is
+// returned.  Fills the effective 64-bit strides of Q, K, V, O.
+int validate(const fa_fwd_params* p, Strides* st) {
+  if (p == nullptr) return fail(FA_ERR_BAD_PARAM, "params is NULL");
+  if (!p->Q || !p->K || !p->V || !p->O) return fail(FA_ERR_BAD_PARAM, "Q, K, V and O must be non-NULL");
+  if (p->dtype != FA_DTYPE_F16 && p->dtype != FA_DTYPE_BF16)
+    return fail(FA_ERR_UNSUPPORTED, "dtype %d is not FA_DTYPE_F16 or FA_DTYPE_BF16", p->dtype);
+  const int d = p->head_dim;
+  if (d != 32 && d != 64 && d != 128) return fail(FA_ERR_UNSUPPORTED, "head_dim %d not in {32, 64, 128}", d);
+  if (p->batch < 1 || p->heads < 1 || p->seq_len < 1)
+    return fail(FA_ERR_BAD_SHAPE, "batch (%d), heads (%d) and seq_len (%d) must be >= 1", p->batch, p->heads,
+                p->seq_len);
+  if (!(std::isfinite(p->softmax_scale) && p->softmax_scale > 0.f))
+    return fail(FA_ERR_BAD_PARAM, "softmax_scale must be finite and > 0 (got %g)", double(p->softmax_scale));
+  if (p->causal != 0 && p->causal != 1) return fail(FA_ERR_BAD_PARAM, "causal must be 0 or 1");
+  const int n = p->seq_len, h = p->heads, b = p->batch;
+  const void* bases[4] = {p->Q, p->K, p->V, p->O};
+  const char* names[4] = {"Q", "K", "V", "O"};
+  const int seq_s[4] = {p->stride_seq_q, p->stride_seq_k, p->stride_seq_v, p->stride_seq_o};
+  const int head_s[4] = {p->stride_head_q, p->stride_head_k, p->stride_head_v, p->stride_head_o};
+  const int batch_s[4] = {p->stride_batch_q, p->stride_batch_k, p->stride_batch_v, p->stride_batch_o};
+  int64_t* ss = st->seq;
+  int64_t* hs = st->head;
+  int64_t* bs = st->batch;
+  for (int i = 0; i < 4; ++i) {
+    if (!aligned16(bases[i])) return fail(FA_ERR_BAD_ALIGN, "%s is not 16-byte aligned", names[i]);
+    ss[i] = seq_s[i];
+    hs[i] = pick(p->stride_head64[i], head_s[i]);
+    bs[i] = pick(p->stride_batch64[i], batch_s[i]);
+    if (ss[i] < d) return fail(FA_ERR_BAD_SHAPE, "stride_seq of %s (%lld) < head_dim", names[i], (long long)ss[i]);
+    if ((h > 1 && hs[i] < 1) || (b > 1 && bs[i] < 1))
+      return fail(FA_ERR_BAD_SHAPE, "head/batch strides of %s must be positive", names[i]);
+    const int64_t chk[3] = {ss[i], h > 1 ? hs[i] : 8, b > 1 ? bs[i] : 8};
+    for (int k = 0; k < 3; ++k)
+      if (chk[k] % 8 != 0)
+        return fail(FA_ERR_BAD_ALIGN, "strides of %s must be multiples of 8 elements (16 bytes)", names[i]);
+    for (int k = 0; k < 3; ++k)
+      if (chk[k] >= kMaxStride)
+        return fail(FA_ERR_BAD_SHAPE, "a stride of %s is 2^40 bytes or more (the TMA limit)", names[i]);
+    const __int128 extent = __int128(b - 1) * (b > 1 ? bs[i] : 0) + __int128(h - 1) * (h > 1 ? hs[i] : 0) +
+                            __int128(n - 1) * ss[i] + d;
+    if (extent > kMaxExtent) return fail(FA_ERR_BAD_SHAPE, "%s spans more than 2^48 bytes", names[i]);
+  }
+  if (p->LSE && (reinterpret_cast<uintptr_t>(p->LSE) & 3u)) return fail(FA_ERR_BAD_ALIGN, "LSE not 4-byte aligned");
+  return FA_OK;
+}
+
+
 }  // namespace
 
 namespace fa {
 void set_last_error(const char* msg) { g_last_error = msg; }
+
+int validate_params(const fa_fwd_params* p) {
+  g_last_error.clear();
+  Strides st;
+  return validate(p, &st);
+}
 }  // namespace fa
 
 extern "C" {
@@ -152,39 +217,14 @@ const char* fa_last_error(void) { return g_last_error.c_str(); }
 
 int fa_fwd_sm100(const fa_fwd_params* p, void* stream_ptr) {
   g_last_error.clear();
-  if (p == nullptr) return fail(FA_ERR_BAD_PARAM, "params is NULL");
-  if (!p->Q || !p->K || !p->V || !p->O) return fail(FA_ERR_BAD_PARAM, "Q, K, V and O must be non-NULL");
-  if (p->dtype != FA_DTYPE_F16 && p->dtype != FA_DTYPE_BF16)
-    return fail(FA_ERR_UNSUPPORTED, "dtype %d is not FA_DTYPE_F16 or FA_DTYPE_BF16", p->dtype);
+  Strides st;
+  const int vrc = validate(p, &st);
+  if (vrc != FA_OK) return vrc;
   const int d = p->head_dim;
-  if (d != 32 && d != 64 && d != 128) return fail(FA_ERR_UNSUPPORTED, "head_dim %d not in {32, 64, 128}", d);
-  if (p->batch < 1 || p->heads < 1 || p->seq_len < 1)
-    return fail(FA_ERR_BAD_SHAPE, "batch (%d), heads (%d) and seq_len (%d) must be >= 1", p->batch, p->heads,
-                p->seq_len);
-  if (!(std::isfinite(p->softmax_scale) && p->softmax_scale > 0.f))
-    return fail(FA_ERR_BAD_PARAM, "softmax_scale must be finite and > 0 (got %g)", double(p->softmax_scale));
-  if (p->causal != 0 && p->causal != 1) return fail(FA_ERR_BAD_PARAM, "causal must be 0 or 1");
   const int n = p->seq_len, h = p->heads, b = p->batch;
-  const void* bases[4] = {p->Q, p->K, p->V, p->O};
-  const char* names[4] = {"Q", "K", "V", "O"};
-  const int seq_s[4] = {p->stride_seq_q, p->stride_seq_k, p->stride_seq_v, p->stride_seq_o};
-  const int head_s[4] = {p->stride_head_q, p->stride_head_k, p->stride_head_v, p->stride_head_o};
-  const int batch_s[4] = {p->stride_batch_q, p->stride_batch_k, p->stride_batch_v, p->stride_batch_o};
-  int64_t ss[4], hs[4], bs[4];
-  for (int i = 0; i < 4; ++i) {
-    if (!aligned16(bases[i])) return fail(FA_ERR_BAD_ALIGN, "%s is not 16-byte aligned", names[i]);
-    ss[i] = seq_s[i];
-    hs[i] = pick(p->stride_head64[i], head_s[i]);
-    bs[i] = pick(p->stride_batch64[i], batch_s[i]);
-    if (ss[i] < d) return fail(FA_ERR_BAD_SHAPE, "stride_seq of %s (%lld) < head_dim", names[i], (long long)ss[i]);
-    if ((h > 1 && hs[i] < 1) || (b > 1 && bs[i] < 1))
-      return fail(FA_ERR_BAD_SHAPE, "head/batch strides of %s must be positive", names[i]);
-    const int64_t chk[3] = {ss[i], h > 1 ? hs[i] : 8, b > 1 ? bs[i] : 8};
-    for (int k = 0; k < 3; ++k)
-      if (chk[k] % 8 != 0)
-        return fail(FA_ERR_BAD_ALIGN, "strides of %s must be multiples of 8 elements (16 bytes)", names[i]);
-  }
-  if (p->LSE && (reinterpret_cast<uintptr_t>(p->LSE) & 3u)) return fail(FA_ERR_BAD_ALIGN, "LSE not 4-byte aligned");
+  const int64_t* ss = st.seq;
+  const int64_t* hs = st.head;
+  const int64_t* bs = st.batch;
 
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return fail(FA_ERR_UNSUPPORTED, "no CUDA device");

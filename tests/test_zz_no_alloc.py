@@ -146,7 +146,21 @@ def test_noalloc_rejects_a_workspace():
     lib = _lib.load()
     lib.fa_fwd_sm100_noalloc.argtypes = [ctypes.POINTER(_lib.FwdParams), ctypes.c_void_p]
     lib.fa_fwd_sm100_noalloc.restype = ctypes.c_int
-    p = _lib.FwdParams()
-    p.workspace = 0x1000
+    # Valid arguments on real device buffers, plus a caller workspace: the
+    # workspace alone is the error, and nothing launches.
+    dev = torch.device("cuda", 0)
+    shape = (1, 2, 256, 64)
+    q, k, v = (t.to(dev) for t in make_random(shape, torch.float16, seed=3))
+    o = torch.empty_like(q)
+    lse = torch.empty(shape[:3], dtype=torch.float32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws = torch.zeros(256, dtype=torch.uint8, device=dev)
+    p = _params(q, k, v, o, lse, 0.125, False, status)
+    p.workspace = ws.data_ptr()
+    p.workspace_bytes = 256
     assert lib.fa_fwd_sm100_noalloc(ctypes.byref(p), None) == _lib.FA_ERR_BAD_PARAM
     assert b"workspace" in lib.fa_last_error()
+    # Bad arguments are reported as such before the workspace is looked at.
+    p.head_dim = 96
+    assert lib.fa_fwd_sm100_noalloc(ctypes.byref(p), None) == _lib.FA_ERR_UNSUPPORTED
+    assert b"head_dim" in lib.fa_last_error()
