@@ -212,8 +212,9 @@ def run_reference_arm(args, cfg: AttnConfig):
     from oracle import oracle as orc
 
     use_ref, kind = cpu_kind()
-    threads = orc.host_threads()
-    n_slices = threads  # one slice per host thread per step
+    # one slice per host thread per step, at most the workload's own slice count
+    threads = min(orc.host_threads(), cfg.slices)
+    n_slices = threads
     # A step takes seconds on the CPU: run at most three warm-up steps, and only
     # as many timed steps as fit in REF_BUDGET_S (the line reports the steps run).
     warm = min(args.warmup, 3)
@@ -225,7 +226,7 @@ def run_reference_arm(args, cfg: AttnConfig):
     times = [cpu_sample(cfg, n_slices, threads, use_ref) for _ in range(steps)]
     t = float(np.mean(times))
     value = cfg.flops(n_slices) / t / 1e12
-    sample = (f"{n_slices} of {cfg.slices} (b,h) slices of {cfg.name} per step "
+    sample = (f"{n_slices} of the {cfg.slices} (b,h) slices of {cfg.name} per step "
               f"(N={cfg.seq_len}, d={cfg.head_dim}, causal={cfg.causal}), one per host thread")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world,
@@ -241,6 +242,28 @@ def run_reference_arm(args, cfg: AttnConfig):
 
 # ----------------------------------------------------------------------------- GPU leg
 
+L2_BYTES = 126 * 2 ** 20
+FLUSH_BYTES = 256 * 2 ** 20  # written between timed launches when the inputs could stay in L2
+
+
+def rank_bytes(cfg: AttnConfig, world: int, scaling: str) -> int:
+    """Q, K, V and O bytes one rank holds."""
+    slices = cfg.slices if scaling == "weak" else -(-cfg.slices // world)
+    return 4 * slices * cfg.seq_len * cfg.head_dim * 2
+
+
+def needs_flush(cfg: AttnConfig, world: int, scaling: str) -> bool:
+    return rank_bytes(cfg, world, scaling) < 2 * L2_BYTES
+
+
+def l2_note(cfg: AttnConfig, world: int, scaling: str) -> str:
+    mb = rank_bytes(cfg, world, scaling) / 1e6
+    if needs_flush(cfg, world, scaling):
+        return (f"L2 flushed before every timed launch (a {FLUSH_BYTES >> 20} MiB write, outside the launch's "
+                f"events): Q+K+V+O per rank is {mb:.0f} MB, under twice the 126 MB L2")
+    return f"inputs larger than L2 (Q+K+V+O per rank {mb:.0f} MB against 126 MB); no flush needed"
+
+
 def workload_config(cfg: AttnConfig, world: int, scaling: str):
     per_rank_b = cfg.batch if scaling == "weak" else cfg.batch  # slices split below for strong
     return {
@@ -248,7 +271,7 @@ def workload_config(cfg: AttnConfig, world: int, scaling: str):
         "global_batch": cfg.batch * world if scaling == "weak" else cfg.batch,
         "heads": cfg.heads, "seq_len": cfg.seq_len, "head_dim": cfg.head_dim, "causal": cfg.causal,
         "input_dtype": str(cfg.dtype).replace("torch.", ""), "parallelism": f"bh-shard x{world}",
-        "l2": "inputs larger than L2 (Q+K+V per rank >> 126 MB); no flush needed",
+        "l2": l2_note(cfg, world, scaling),
         "lse": True,
     }
 
@@ -326,18 +349,25 @@ def run_ours(args, cfg: AttnConfig):
     torch.cuda.synchronize(dev)
     barrier()
     torch.cuda.synchronize(dev)
+    flush = (torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+             if needs_flush(cfg, world, args.scaling) else None)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     t_wall0 = time.time()
     for i in range(args.steps):
+        if flush is not None:
+            flush.fill_(i & 0xFF)  # evicts the previous launch's inputs and outputs from L2
         starts[i].record(stream)
         step()
         ends[i].record(stream)
     torch.cuda.synchronize(dev)
     t_wall1 = time.time()
     barrier()
-    total_ms = starts[0].elapsed_time(ends[-1])
     launch_ms = float(np.mean([s.elapsed_time(e) for s, e in zip(starts, ends)]))
+    # With a flush between launches a step is one launch; without, back-to-back
+    # launches are timed end to end.
+    total_ms = launch_ms * args.steps if flush is not None else starts[0].elapsed_time(ends[-1])
+    del flush
     sampler.stop()
     status = fa.device_status(dev)
     if status != 0:
@@ -428,7 +458,7 @@ def run_ours(args, cfg: AttnConfig):
             from oracle import oracle as orc
 
             use_ref, kind = cpu_kind()
-            threads = orc.host_threads()
+            threads = min(orc.host_threads(), cfg.slices)
             n_cpu = max(1, threads)
             secs = cpu_sample(cfg, n_cpu, threads, use_ref)
             cpu = {"value": cfg.flops(n_cpu) / secs / 1e12, "unit": "TFLOPS", "cores": threads, "kind": kind,

@@ -1,0 +1,68 @@
+"""CPU checks of bench.py's output contract.
+
+The reference arm (the reference's CPU attention, compiled from its sources into
+oracle/_ref, or the restated oracle where that build is absent) runs here without
+a GPU and must print exactly one JSON line with the fields the harness reads.
+Our arm must fail loudly without a GPU rather than print a number.  The L2 policy
+flushes between timed launches exactly when a rank's tensors could stay in L2.
+"""
+from __future__ import annotations
+
+import json
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _bench(*args, timeout=600):
+    return subprocess.run([sys.executable, str(ROOT / "bench.py"), *map(str, args)], capture_output=True,
+                          text=True, timeout=timeout, cwd=ROOT)
+
+
+def test_reference_arm_prints_one_contract_line():
+    r = _bench("--impl", "reference", "--workload", "cfg0", "--steps", 2, "--warmup", 1)
+    assert r.returncode == 0, r.stderr
+    lines = r.stdout.strip().splitlines()
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert key in d, key
+    assert d["impl"] == "reference" and d["unit"] == "TFLOPS" and d["higher_is_better"] is True
+    assert d["value"] > 0 and d["n_gpus"] == 1 and d["vs_baseline"] is None
+    assert d["config"]["workload"] == "cfg0"
+    cb = d["cpu_baseline"]
+    assert cb["value"] == d["value"] and cb["kind"] in ("reference", "port")
+    assert 1 <= cb["cores"] <= 4  # cfg0 has 4 (b,h) slices: no more threads than slices
+    assert cb["sample"].startswith(f"{cb['cores']} of the 4 (b,h) slices of cfg0")
+    assert d["e2e"] == {"value": d["value"], "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    assert "flushed" in d["config"]["l2"]
+
+
+def test_our_arm_fails_loudly_without_a_gpu():
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    r = _bench("--workload", "cfg0", "--steps", 2, "--warmup", 1)
+    assert r.returncode != 0
+    assert r.stdout.strip() == ""
+
+
+def test_l2_flush_policy():
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    from flash_attention_runtime.inputs import CONFIGS
+
+    flushed = {name for name, cfg in CONFIGS.items() if bench.needs_flush(cfg, 1, "weak")}
+    assert {"cfg0", "cfg1", "cfg4_d32"} <= flushed
+    assert not flushed & {"cfg2", "cfg3", "cfg4_d128"}
+    # Strong scaling splits the slices: at 8 ranks configuration 2 is 134 MB per rank.
+    assert bench.needs_flush(CONFIGS["cfg2"], 8, "strong")
+    assert not bench.needs_flush(CONFIGS["cfg2"], 8, "weak")
+    assert bench.rank_bytes(CONFIGS["cfg2"], 1, "weak") == 4 * 8 * 32 * 4096 * 128 * 2
+    assert "no flush" in bench.l2_note(CONFIGS["cfg2"], 1, "weak")
