@@ -1,9 +1,13 @@
-"""CPU tests of the (batch x head) sharding and the verification gather.
+"""Tests of the (batch x head) sharding and the verification gather.
 
-Two gloo ranks on CPU each take their slices of the same seeded inputs, run the
+On CPU, two gloo ranks each take their slices of the same seeded inputs, run the
 CPU oracle on them (standing in for the GPU kernel, whose per-slice results are
 independent of the other slices) and all-gather O and LSE; the gathered result
 must be bit-identical to the oracle over the whole batch.
+
+On a box with two or more GPUs, two NCCL ranks run the kernel on their slices,
+one GPU each, and all-gather O and LSE; the gathered result must match the
+oracle within the parity tolerances.
 """
 from __future__ import annotations
 
@@ -79,4 +83,49 @@ def _worker(rank, world, port, result_path):
 def test_two_rank_gloo_shard_and_gather(tmp_path):
     out = tmp_path / "result.txt"
     mp.start_processes(_worker, args=(2, _free_port(), str(out)), nprocs=2, join=True, start_method="spawn")
+    assert out.read_text() == "ok"
+
+
+def _gpu_worker(rank, world, port, result_path):
+    for p in (str(ROOT), str(ROOT / "flash-attention_b200"), str(ROOT / "tests")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import datetime
+
+    import flash_attention_runtime as fa
+    from flash_attention_runtime.inputs import make_random
+    from flash_attention_runtime.sharding import gather as g, shard as sh
+    from oracle.oracle import oracle_attention
+    from parity import compare_lse, compare_output
+
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        shape, scale = (2, 3, 300, 64), 0.125
+        q, k, v = make_random(shape, torch.bfloat16, seed=14)
+        s = shape[0] * shape[1]
+        ql, kl, vl = (sh(t.contiguous(), rank, world).to(dev) for t in (q, k, v))
+        o, lse = fa.forward(ql, kl, vl, softmax_scale=scale, causal=True, return_lse=True)
+        o_all = g(o, s)
+        l_all = g(lse, s)
+        torch.cuda.synchronize(dev)
+        if rank == 0:
+            o_ref, l_ref = oracle_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), scale, True)
+            ro = compare_output(o_all, o_ref.reshape(s, *shape[2:]), torch.bfloat16)
+            rl = compare_lse(l_all, l_ref.reshape(s, shape[2]))
+            Path(result_path).write_text("ok" if ro["ok"] and rl["ok"] else f"mismatch {ro} {rl}")
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_two_gpu_nccl_shard_and_gather(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    out = tmp_path / "result.txt"
+    mp.start_processes(_gpu_worker, args=(2, _free_port(), str(out)), nprocs=2, join=True, start_method="spawn")
     assert out.read_text() == "ok"
