@@ -2,16 +2,23 @@
 """Benchmark of the sm_100a FlashAttention-2 forward (the hot path) - driver contract.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload cfg2] [--scaling weak|strong]
+                    [--workload cfg2] [--scaling strong|weak]
 
 A step is one forward over one batch of synthetic seeded input (configuration 2
 by default: B8 H32 N4096 d128 bf16 causal, the configuration the headline target
-is quoted on), O and the logsumexp written.  Under torchrun each rank is one GPU;
-ranks process independent (batch x head) slices with no collective on the data
-path ("weak": every rank runs a full configuration-2 batch of its own slices;
-"strong": the configuration's slices are split across ranks).  Timing: W warm-up
-steps, then K steps between a barrier + synchronize on each side, device time from
-CUDA events on the launching stream, max over ranks.  Rank 0 prints one JSON line.
+is quoted on), O and the logsumexp written.  Under torchrun each rank is one GPU.
+By default ("strong") the configuration's B*H (batch, head) slices are split
+across the ranks, rank r taking slices [r*S/N, (r+1)*S/N): the same total work at
+every N, with no collective on the data path.  ("weak": every rank runs a full
+batch of its own slices.)  Timing: W warm-up steps, then K steps between a
+barrier + synchronize on each side, device time from CUDA events on the launching
+stream, max over ranks.  `value` is the whole job's TFLOPS (all ranks' FLOPs over
+the slowest rank's time); `per_gpu` is value / N.
+
+After the timed region the ranks all-gather O and LSE (NCCL over NVLink) and rank
+0 checks a strided set of slices of the gathered result against a float64
+evaluation of softmax(scale * Q K^T [causal]) V on its GPU; the line carries the
+result under `parity`, and a failed check makes the run exit non-zero.
 
 `--impl reference` times the reference's own CPU attention
 (benchmark/cpp/correctness_v6.cu:23-72, built from its sources into oracle/_ref)
@@ -42,26 +49,33 @@ import torch  # noqa: E402
 
 from flash_attention_runtime.inputs import CONFIGS, AttnConfig  # noqa: E402
 
-METRIC = "attention fwd TFLOPS/GPU (4*B*H*N^2*d/t, halved for causal)"
+METRIC = ("attention fwd TFLOPS of the whole job over n_gpus (4*B*H*N^2*d/t, halved for causal); "
+          "per_gpu = value/n_gpus, and % of dense bf16 peak in roofline")
 REF_BUDGET_S = 150.0
+E2E_BUDGET_S = 10.0   # the end-to-end leg runs min(--steps, what fits in this) steps
 E2E_CHUNKS = 8
+SUSTAINED_AFTER_S = 1.0  # timed regions at least this long are compared with the sustained peak
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+ATOL = {torch.float16: 2e-3, torch.bfloat16: 1e-2}
+LSE_RTOL = 1e-4
 
 
-def parse_args():
+def parse_args(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=1000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="cfg2", choices=sorted(CONFIGS))
-    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="strong")
     ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--verify-slices", type=int, default=8,
+                    help="slices of the gathered output checked against float64 (0: no check)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-device", choices=["cpu", "gpu"], default="cpu",
                     help="with --impl reference: gpu times the reference's own CUDA kernel instead "
                          "(fp16, d=128, non-causal workloads only, e.g. cfg4_d128 or cfg2_f16nc)")
-    return ap.parse_args()
+    return ap.parse_args(argv)
 
 
 def load_peaks():
@@ -72,9 +86,28 @@ def load_peaks():
     return dict(FALLBACK_PEAKS), "fallback"
 
 
+def pick_peak(peaks: dict, timed_region_s: float):
+    """Dense bf16 peak to divide by: the burst figure for a timed region shorter
+    than SUSTAINED_AFTER_S (the GPU has not settled at its power cap yet), the
+    sustained one for a seconds-long region."""
+    if timed_region_s >= SUSTAINED_AFTER_S:
+        return float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])), \
+            "bf16_tflops_sustained"
+    return float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])), "bf16_tflops"
+
+
 def dist_env():
     return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
             int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def check_slices(num_slices: int, count: int):
+    """Slices 0 and S-1 plus evenly strided ones in between, `count` in all."""
+    if count <= 0 or num_slices <= 0:
+        return []
+    if count >= num_slices:
+        return list(range(num_slices))
+    return sorted({round(i * (num_slices - 1) / (count - 1)) for i in range(count)} if count > 1 else {0})
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -138,20 +171,26 @@ class ClockSampler:
 
 # ----------------------------------------------------------------------------- CPU leg
 
-def cpu_sample(cfg: AttnConfig, n_slices: int, threads: int, use_ref: bool):
-    """Time the CPU attention on `n_slices` (b,h) slices of cfg; returns (seconds, kind)."""
+def cpu_sample(cfg: AttnConfig, q: np.ndarray, k: np.ndarray, v: np.ndarray, threads: int, use_ref: bool):
+    """Run the CPU attention on [1, S, N, d] float32 slices; returns (seconds, O)."""
     from oracle import oracle as orc
 
-    g = torch.Generator(device="cpu")
-    g.manual_seed(cfg.seed)
-    shape = (1, n_slices, cfg.seq_len, cfg.head_dim)
-    q, k, v = (torch.randn(shape, generator=g).to(cfg.dtype).float().numpy() for _ in range(3))
     t0 = time.perf_counter()
     if use_ref:
-        orc.ref_attention(q, k, v, cfg.scale, cfg.causal, threads=threads)
+        o = orc.ref_attention(q, k, v, cfg.scale, cfg.causal, threads=threads)
     else:
-        orc.oracle_attention(q, k, v, cfg.scale, cfg.causal, threads=threads)
-    return time.perf_counter() - t0
+        o, _ = orc.oracle_attention(q, k, v, cfg.scale, cfg.causal, threads=threads)
+    return time.perf_counter() - t0, o
+
+
+def cpu_inputs(cfg: AttnConfig, n_slices: int):
+    """The first `n_slices` (b,h) slices of the workload's seeded inputs, as float32 numpy."""
+    from flash_attention_runtime.inputs import generate
+
+    q, k, v = generate(cfg)
+    s = cfg.slices
+    return tuple(t.reshape(1, s, cfg.seq_len, cfg.head_dim)[:, :n_slices].float().contiguous().numpy()
+                 for t in (q, k, v))
 
 
 def cpu_kind():
@@ -168,7 +207,7 @@ def run_reference_gpu(args, cfg: AttnConfig):
     from oracle import oracle as orc
 
     base = {"impl": "reference", "device": "gpu", "metric": METRIC, "unit": "TFLOPS", "higher_is_better": True,
-            "config": workload_config(cfg, 1, "weak"),
+            "config": workload_config(cfg, 1, "strong"),
             "kernel": "flash_attention_forward_v6_mma (src/forward/forward_v6_mma.cuh:325-412), mma.sync, sm_100"}
     why = None
     if cfg.dtype != torch.float16 or cfg.head_dim != 128 or cfg.causal or cfg.seq_len % 64:
@@ -215,15 +254,16 @@ def run_reference_arm(args, cfg: AttnConfig):
     # one slice per host thread per step, at most the workload's own slice count
     threads = min(orc.host_threads(), cfg.slices)
     n_slices = threads
+    q, k, v = cpu_inputs(cfg, n_slices)
     # A step takes seconds on the CPU: run at most three warm-up steps, and only
     # as many timed steps as fit in REF_BUDGET_S (the line reports the steps run).
     warm = min(args.warmup, 3)
     times = []
     for _ in range(warm):
-        times.append(cpu_sample(cfg, n_slices, threads, use_ref))
+        times.append(cpu_sample(cfg, q, k, v, threads, use_ref)[0])
     est = float(np.median(times)) if times else None
     steps = args.steps if est is None else max(1, min(args.steps, int(REF_BUDGET_S / max(est, 1e-3))))
-    times = [cpu_sample(cfg, n_slices, threads, use_ref) for _ in range(steps)]
+    times = [cpu_sample(cfg, q, k, v, threads, use_ref)[0] for _ in range(steps)]
     t = float(np.mean(times))
     value = cfg.flops(n_slices) / t / 1e12
     sample = (f"{n_slices} of the {cfg.slices} (b,h) slices of {cfg.name} per step "
@@ -246,10 +286,14 @@ L2_BYTES = 126 * 2 ** 20
 FLUSH_BYTES = 256 * 2 ** 20  # written between timed launches when the inputs could stay in L2
 
 
+def rank_slices(cfg: AttnConfig, world: int, scaling: str) -> int:
+    """Most (b,h) slices any rank holds."""
+    return cfg.slices if scaling == "weak" else -(-cfg.slices // world)
+
+
 def rank_bytes(cfg: AttnConfig, world: int, scaling: str) -> int:
     """Q, K, V and O bytes one rank holds."""
-    slices = cfg.slices if scaling == "weak" else -(-cfg.slices // world)
-    return 4 * slices * cfg.seq_len * cfg.head_dim * 2
+    return 4 * rank_slices(cfg, world, scaling) * cfg.seq_len * cfg.head_dim * 2
 
 
 def needs_flush(cfg: AttnConfig, world: int, scaling: str) -> bool:
@@ -265,38 +309,94 @@ def l2_note(cfg: AttnConfig, world: int, scaling: str) -> str:
 
 
 def workload_config(cfg: AttnConfig, world: int, scaling: str):
-    per_rank_b = cfg.batch if scaling == "weak" else cfg.batch  # slices split below for strong
+    strong = scaling == "strong"
     return {
-        "workload": cfg.name, "batch_per_rank": per_rank_b if scaling == "weak" else None,
-        "global_batch": cfg.batch * world if scaling == "weak" else cfg.batch,
+        "workload": cfg.name,
+        "batch_per_rank": None if strong else cfg.batch,
+        "global_batch": cfg.batch if strong else cfg.batch * world,
         "heads": cfg.heads, "seq_len": cfg.seq_len, "head_dim": cfg.head_dim, "causal": cfg.causal,
-        "input_dtype": str(cfg.dtype).replace("torch.", ""), "parallelism": f"bh-shard x{world}",
+        "input_dtype": str(cfg.dtype).replace("torch.", ""),
+        "slices": cfg.slices if strong else cfg.slices * world,
+        "slices_per_rank": rank_slices(cfg, world, scaling),
+        "parallelism": (f"bh-shard x{world}: rank r owns (b,h) slices [r*S/{world}, (r+1)*S/{world})" if strong
+                        else f"bh-shard x{world}: every rank a full batch of its own slices"),
         "l2": l2_note(cfg, world, scaling),
         "lse": True,
     }
 
 
-def rank_inputs(cfg: AttnConfig, rank: int, world: int, scaling: str, dev):
-    """This rank's Q, K, V on `dev` (drawn on the CPU, seeded per rank)."""
+def rank_inputs(cfg: AttnConfig, rank: int, world: int, scaling: str):
+    """This rank's Q, K, V (CPU, drawn seeded) as [1, S_r, N, d] for strong scaling
+    or the full [B, H, N, d] of its own seed for weak; plus (full q, k, v or None,
+    first slice index)."""
     from flash_attention_runtime.inputs import generate
+    from flash_attention_runtime.sharding import slice_range
 
     if scaling == "weak":
         q, k, v = generate(cfg, seed_offset=1000 * rank)
-        n_slices = cfg.slices
-    else:
-        q, k, v = generate(cfg)
-        s = cfg.slices
-        lo, hi = rank * s // world, (rank + 1) * s // world
-        flat = lambda t: t.reshape(s, cfg.seq_len, cfg.head_dim)[lo:hi]  # noqa: E731
-        q, k, v = (flat(t).reshape(1, hi - lo, cfg.seq_len, cfg.head_dim).contiguous() for t in (q, k, v))
-        n_slices = hi - lo
-    return q, k, v, n_slices
+        return (q, k, v), (q, k, v), 0
+    q, k, v = generate(cfg)
+    s = cfg.slices
+    lo, hi = slice_range(s, rank, world)
+    part = tuple(t.reshape(1, s, cfg.seq_len, cfg.head_dim)[:, lo:hi].contiguous() for t in (q, k, v))
+    return part, (q, k, v), lo
+
+
+def reference_slice(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, causal: bool):
+    """float64 softmax(scale * q k^T [causal]) v and its natural-log logsumexp, for
+    one [N, d] slice on q's device: the checker for the gathered output."""
+    qd, kd, vd = q.double(), k.double(), v.double()
+    s = (qd @ kd.transpose(0, 1)) * scale
+    if causal:
+        n = s.shape[0]
+        s.masked_fill_(torch.ones(n, n, dtype=torch.bool, device=s.device).triu_(1), float("-inf"))
+    m = s.amax(dim=1, keepdim=True)
+    p = torch.exp(s - m)
+    l = p.sum(dim=1, keepdim=True)
+    o = (p @ vd) / l
+    return o, (m + torch.log(l)).squeeze(1)
+
+
+def half_ulp(x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """Half the spacing of `dtype` numbers at |x| (normal range)."""
+    mant = {torch.float16: 10, torch.bfloat16: 7}[dtype]
+    e = torch.floor(torch.log2(x.abs().clamp(min=2.0 ** -14)))
+    return torch.exp2(e - mant - 1)
+
+
+def verify(cfg: AttnConfig, full, o_all: torch.Tensor, lse_all: torch.Tensor, slices, dev):
+    """Check `slices` of the gathered O / LSE ([S, N, d] / [S, N]) against float64."""
+    q, k, v = full  # [B, H, N, d] on the CPU
+    flat = lambda t: t.reshape(cfg.slices, cfg.seq_len, cfg.head_dim)  # noqa: E731
+    qf, kf, vf = flat(q), flat(k), flat(v)
+    atol = ATOL[cfg.dtype]
+    max_abs = max_rounded = lse_rel = worst_excess = 0.0
+    for i in slices:
+        ro, rl = reference_slice(qf[i].to(dev), kf[i].to(dev), vf[i].to(dev), cfg.scale, cfg.causal)
+        out = o_all[i].to(dev).double()
+        err = (out - ro).abs()
+        max_abs = max(max_abs, float(err.max()))
+        max_rounded = max(max_rounded, float((out - ro.to(cfg.dtype).double()).abs().max()))
+        worst_excess = max(worst_excess, float((err - atol - half_ulp(ro, cfg.dtype)).max()))
+        lr = lse_all[i].to(dev).double()
+        lse_rel = max(lse_rel, float(((lr - rl).abs() / rl.abs().clamp(min=1.0)).max()))
+        del ro, rl, out, err
+    finite = bool(torch.isfinite(o_all).all()) and bool(torch.isfinite(lse_all).all())
+    return {
+        "checker": "float64 softmax(scale*QK^T)V and logsumexp on rank 0's GPU",
+        "slices": list(slices), "max_abs": max_abs, "max_abs_vs_ref_rounded_to_dtype": max_rounded,
+        "bound": atol, "bound_rule": "|dO| <= bound + half an output ulp of the reference, per element",
+        "worst_excess_over_bound": worst_excess, "lse_max_rel": lse_rel, "lse_bound": LSE_RTOL,
+        "all_finite": finite,
+        "ok": finite and worst_excess <= 0.0 and lse_rel <= LSE_RTOL,
+    }
 
 
 def run_ours(args, cfg: AttnConfig):
     import torch.distributed as dist
 
     import flash_attention_runtime as fa
+    from flash_attention_runtime.sharding import gather
 
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
@@ -332,7 +432,8 @@ def run_ours(args, cfg: AttnConfig):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    qh, kh, vh, n_slices = rank_inputs(cfg, rank, world, args.scaling, dev)
+    (qh, kh, vh), full, first_slice = rank_inputs(cfg, rank, world, args.scaling)
+    n_slices = qh.shape[0] * qh.shape[1]
     q, k, v = qh.to(dev), kh.to(dev), vh.to(dev)
     o = torch.empty_like(q)
     lse = torch.empty(q.shape[:3], dtype=torch.float32, device=dev)
@@ -344,7 +445,8 @@ def run_ours(args, cfg: AttnConfig):
     fa.reset_device_status(dev)
     sampler = ClockSampler(local)
     sampler.start()
-    for _ in range(max(args.warmup, 3)):
+    warmup = max(args.warmup, 3)
+    for _ in range(warmup):
         step()
     torch.cuda.synchronize(dev)
     barrier()
@@ -378,14 +480,34 @@ def run_ours(args, cfg: AttnConfig):
     flops_rank = cfg.flops(n_slices)
     total_flops = flops_rank * world if args.scaling == "weak" else cfg.flops()
     value = total_flops / (ms_per_step * 1e-3) / 1e12
+    timed_region_s = ms_per_step * args.steps / 1e3
+
+    # ---- verification: gather O and LSE (NCCL all-gather; local at one rank) and
+    # check strided slices of the whole result against float64 on rank 0.
+    parity = None
+    if args.verify_slices > 0:
+        s_total = cfg.slices  # strong: the whole configuration; weak: rank 0's own batch
+        o_loc = o.reshape(1, n_slices, cfg.seq_len, cfg.head_dim)
+        l_loc = lse.reshape(1, n_slices, cfg.seq_len)
+        if args.scaling == "strong" and world > 1:
+            o_all = gather(o_loc, s_total)
+            l_all = gather(l_loc, s_total)
+            gathered = f"NCCL all_gather of O and LSE over {world} ranks"
+        else:
+            o_all, l_all = o_loc[0], l_loc[0]  # weak: each rank checks its own batch
+            gathered = "local (one rank holds every slice)" if world == 1 else "local (weak scaling, rank 0's batch)"
+        torch.cuda.synchronize(dev)
+        if rank == 0:
+            parity = verify(cfg, full, o_all, l_all, check_slices(s_total, args.verify_slices), dev)
+            parity["gathered"] = gathered
+        del o_all, l_all
+        barrier()
 
     # ---- end to end through the public API: pinned host -> device, forward, device -> host.
     # The rank's slices go through in E2E_CHUNKS chunks so the upload of chunk c+1
     # (one copy engine), the forward of chunk c and the download of chunk c-1 (the
     # other copy engine) overlap; events keep buffer reuse across steps ordered.
-    e2e_steps = args.e2e_steps if args.e2e_steps is not None else max(3, min(20, args.steps // 50))
-    e2e_steps = max(1, e2e_steps)
-    s_all = qh.shape[0] * qh.shape[1]
+    s_all = n_slices
     flat = lambda t: t.reshape(1, s_all, *t.shape[2:])  # noqa: E731
     qp, kp, vp = (flat(t).pin_memory() for t in (qh, kh, vh))
     op = torch.empty(qp.shape, dtype=qh.dtype).pin_memory()
@@ -421,10 +543,16 @@ def run_ours(args, cfg: AttnConfig):
                 ev_out[c].record(down)
         stream.wait_stream(down)
 
-    warm = torch.cuda.Event()
-    warm.record(stream)
-    e2e_step(warm)
+    w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0.record(stream)
+    e2e_step(w0)
+    w1.record(stream)
     torch.cuda.synchronize(dev)
+    warm_ms = max_over_ranks(w0.elapsed_time(w1))
+    if args.e2e_steps is not None:
+        e2e_steps = max(1, args.e2e_steps)
+    else:
+        e2e_steps = max(1, min(args.steps, int(E2E_BUDGET_S * 1e3 / max(warm_ms, 1e-3))))
     barrier()
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -441,13 +569,16 @@ def run_ours(args, cfg: AttnConfig):
     d2h = op.numel() * op.element_size() + lp.numel() * lp.element_size()
 
     peaks, peak_src = load_peaks()
-    peak = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    peak, peak_key = pick_peak(peaks, timed_region_s)
     achieved = flops_rank / (launch_ms_max * 1e-3) / 1e12
     traffic = None
     tfile = ROOT / "profiles" / f"traffic_{cfg.name}.json"
     if tfile.exists():
         try:
+            # per launch of the whole configuration; a rank's launch covers its share of the slices
             traffic = json.loads(tfile.read_text()).get("bytes_per_launch")
+            if traffic is not None:
+                traffic = traffic * n_slices / cfg.slices
         except (ValueError, OSError):
             traffic = None
 
@@ -460,25 +591,38 @@ def run_ours(args, cfg: AttnConfig):
             use_ref, kind = cpu_kind()
             threads = min(orc.host_threads(), cfg.slices)
             n_cpu = max(1, threads)
-            secs = cpu_sample(cfg, n_cpu, threads, use_ref)
+            cq, ck, cv = cpu_inputs(cfg, n_cpu)
+            secs, cpu_o = cpu_sample(cfg, cq, ck, cv, threads, use_ref)
+            # The CPU leg ran the reference's own attention on the workload's first
+            # slices: its output doubles as a check of the GPU output there.
+            gpu_o = o.reshape(n_slices, cfg.seq_len, cfg.head_dim)[:n_cpu].float().cpu().numpy()
             cpu = {"value": cfg.flops(n_cpu) / secs / 1e12, "unit": "TFLOPS", "cores": threads, "kind": kind,
-                   "sample": f"{n_cpu} (b,h) slices of {cfg.name} (N={cfg.seq_len}, d={cfg.head_dim}, "
-                             f"causal={cfg.causal}), one per host thread, {secs:.1f} s"}
+                   "sample": f"the first {n_cpu} (b,h) slices of {cfg.name} (N={cfg.seq_len}, d={cfg.head_dim}, "
+                             f"causal={cfg.causal}), one per host thread, {secs:.1f} s",
+                   "max_abs_vs_gpu": float(np.abs(gpu_o - cpu_o.reshape(gpu_o.shape)).max())}
+        frac_burst = achieved / float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+        frac_sust = achieved / float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
         result = {
-            "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-            "scaling": args.scaling, "vs_baseline": None, "dtype": "bf16" if cfg.dtype == torch.bfloat16 else "f16",
+            "metric": METRIC, "value": value, "unit": "TFLOPS", "per_gpu": value / world, "n_gpus": world,
+            "steps": args.steps, "warmup": warmup, "ms_per_step": ms_per_step, "timed_region_s": timed_region_s,
+            "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
+            "dtype": "bf16" if cfg.dtype == torch.bfloat16 else "f16",
             "data": "synthetic (seeded N(0,1), generated on CPU)",
             "config": workload_config(cfg, world, args.scaling),
+            "parity": parity,
             "e2e": {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms, "steps": e2e_steps, "chunks": n_chunks,
                     "matches_device_timed_output": e2e_ok},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "peak_source": f"{peak_src} bf16_tflops_sustained (kernel timed back to back)",
-                         "frac_of_burst_peak": achieved / float(peaks.get("bf16_tflops", peak)),
+                         "peak_source": (f"{peak_src} {peak_key}: timed region {timed_region_s:.3f} s "
+                                         f"({'at least' if peak_key.endswith('sustained') else 'under'} "
+                                         f"{SUSTAINED_AFTER_S:.0f} s)"),
+                         "frac_of_burst_peak": frac_burst, "frac_of_sustained_peak": frac_sust,
                          "kernel": "fa_fwd_sm100_kernel", "launch_ms": launch_ms_max,
-                         "algorithmic_flops_per_launch": flops_rank},
+                         "algorithmic_flops_per_launch": flops_rank,
+                         "traffic_note": "ncu dram bytes of one whole-configuration launch, scaled by this "
+                                         "rank's share of the slices"},
             "cpu_baseline": cpu,
             "clocks": sampler.summary(t_wall0, t_wall1),
             "gpu_launches": args.steps,
@@ -486,6 +630,8 @@ def run_ours(args, cfg: AttnConfig):
         print(json.dumps(result), flush=True)
     if world > 1:
         dist.destroy_process_group()
+    if rank == 0 and parity is not None and not parity["ok"]:
+        raise SystemExit(f"parity check failed: {parity}")
     return result
 
 

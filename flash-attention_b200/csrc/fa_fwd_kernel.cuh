@@ -211,22 +211,30 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 
 // 2^x for two lanes on the FMA pipe (no MUFU).  Cody-Waite style split
 // x = n + f with n = round-to-nearest(x) (obtained by adding 1.5*2^23, which
-// leaves n in the low mantissa bits), f in [-0.5, 0.5]; 2^f from a degree-4
-// polynomial fitted for this kernel by a Remez exchange for minimax relative
-// error on [-0.5, 0.5] (max relative error 2.6e-6); 2^n applied by adding n to
-// the exponent field.  x is clamped to >= -125 so the result stays a normal
-// number (x = -inf, a masked score, gives 2^-125); callers pass x <= 2^8.
+// leaves n in the low mantissa bits), f in [-0.5, 0.5]; 2^f from the polynomial
+// 1 + f (c1 + f (c2 + f (c3 + f c4))), fitted for this kernel as the minimax
+// relative-error approximation on [-0.5, 0.5] under the constraint p(0) = 1
+// (linear programming on a dense grid; max relative error 2.9e-6 evaluated in
+// fp32); 2^n applied by adding n to the exponent field.  x is clamped to
+// >= -127: a masked score (x = -inf) becomes x = -127, f = 0, p(0) = 1.0, and
+// adding n = -127 to the exponent field of 1.0 gives the bit pattern 0, so P is
+// exactly +0 there, as on the MUFU path (ex2.approx.ftz of -inf).  The same
+// p(0) = 1 makes the row-max element's P exactly 1.  Callers pass x <= 2^8.
+constexpr float kExp2C1 = 0.693124235f;
+constexpr float kExp2C2 = 0.240240902f;
+constexpr float kExp2C3 = 0.0559063852f;
+constexpr float kExp2C4 = 0.00958323106f;
 __device__ __forceinline__ float2 exp2_fma(float2 x) {
   constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
-  x.x = fmaxf(x.x, -125.0f);
-  x.y = fmaxf(x.y, -125.0f);
+  x.x = fmaxf(x.x, -127.0f);
+  x.y = fmaxf(x.y, -127.0f);
   const float2 t = add2(x, make_float2(kShift, kShift));
   const float2 n = add2(t, make_float2(-kShift, -kShift));
   const float2 f = fma2(n, make_float2(-1.0f, -1.0f), x);
-  float2 q = fma2(make_float2(0.009570102f, 0.009570102f), f, make_float2(0.055917859f, 0.055917859f));
-  q = fma2(q, f, make_float2(0.240247443f, 0.240247443f));
-  q = fma2(q, f, make_float2(0.693121791f, 0.693121791f));
-  q = fma2(q, f, make_float2(0.999999285f, 0.999999285f));
+  float2 q = fma2(make_float2(kExp2C4, kExp2C4), f, make_float2(kExp2C3, kExp2C3));
+  q = fma2(q, f, make_float2(kExp2C2, kExp2C2));
+  q = fma2(q, f, make_float2(kExp2C1, kExp2C1));
+  q = fma2(q, f, make_float2(1.0f, 1.0f));
   float2 r;
   r.x = __uint_as_float(__float_as_uint(t.x) * 8388608u + __float_as_uint(q.x));
   r.y = __uint_as_float(__float_as_uint(t.y) * 8388608u + __float_as_uint(q.y));
@@ -424,13 +432,16 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         ok = load_q(0, t) && load_pair(-1, t, 0, t);
         if (ok && t.n1 > 0) ok = load_q(1, t);
         while (ok) {
+          const int nmax = max(t.n0, t.n1);
+          for (int j = 0; ok && j + 1 < nmax; ++j) ok = load_pair(j, t, j + 1, t);
+          if (!ok) break;
+          // Claim the next unit only now, when its first K tile is due (the ring
+          // keeps this thread at most NPAIRS key blocks ahead of the MMAs), so
+          // units are handed out in the order CTAs run out of work.
           const int next = atomicAdd(p.tile_counter, 1) + static_cast<int>(gridDim.x);
           const bool has_next = next < p.num_tiles;
           TileInfo tn = t;
           if (has_next) tn = decode_tile<CAUSAL>(next, p);
-          const int nmax = max(t.n0, t.n1);
-          for (int j = 0; ok && j + 1 < nmax; ++j) ok = load_pair(j, t, j + 1, t);
-          if (!ok) break;
           ok = publish(next);
           if (!ok) break;
           if (!has_next) {
@@ -721,10 +732,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         const float2 neg_mc = make_float2(-mc, -mc);
         float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
         // One loop for every block (one copy of this code in the instruction
-        // cache).  A masked score (-inf) gives x = -inf, which the FMA-pipe exp2
-        // clamps to 2^-125: P is 2^-125 there instead of 0 (0 once rounded to
-        // fp16), 2^125 times below the row's largest P (the element that set the
-        // reference max has P = 1), so it changes no fp32 sum it enters.
+        // cache).  A masked score (-inf) gives x = -inf, and P = 0 exactly on
+        // both exp2 paths (ex2.approx of -inf, and the FMA-pipe exp2's factor 0).
 #pragma unroll
         for (int c = 0; c < kBlockN / 64; ++c) {
           uint32_t pk[32];
@@ -773,6 +782,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }
       if (failed) break;
     }
+    // An abort can leave this warp's last tcgen05.st of P (or of a rescaled O)
+    // in flight; it completes before TMEM is freed after the final barrier.
+    tmem_wait_st();
     tc_fence_before();
   }
 

@@ -24,35 +24,43 @@ void set_last_error(const char* msg);
 // fa_fwd_sm100's device-free argument checks alone (status code, message in
 // fa_last_error()).
 int validate_params(const fa_fwd_params* p);
+// The current device, if it is an sm_100 part (FA_OK), else FA_ERR_UNSUPPORTED /
+// FA_ERR_LAUNCH with the message set; also gives its SM count.
+int current_sm100_device(int* dev, int* sms);
 
 cudaError_t launch_d32(const LaunchSpec& s);
 cudaError_t launch_d64(const LaunchSpec& s);
 cudaError_t launch_d128(const LaunchSpec& s);
 
-// Sets the dynamic-smem attribute of one kernel instantiation once per device.
+// Devices whose "attribute set" flags are cached; on a device past this the
+// attribute is set on every launch (correct, only slower).
+constexpr int kAttrDevices = 64;
+
+// Sets the dynamic-smem attribute of one kernel instantiation once per device
+// (done[dev] records it).
 template <typename Kernel>
-cudaError_t ensure_smem_attr(Kernel k, int smem_bytes, unsigned* done_mask) {
+cudaError_t ensure_smem_attr(Kernel k, int smem_bytes, int (&done)[kAttrDevices]) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  const unsigned bit = 1u << (dev & 31);
-  if (__atomic_load_n(done_mask, __ATOMIC_ACQUIRE) & bit) return cudaSuccess;
+  const bool cached = dev >= 0 && dev < kAttrDevices;
+  if (cached && __atomic_load_n(&done[dev], __ATOMIC_ACQUIRE)) return cudaSuccess;
   e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
   if (e != cudaSuccess) return e;
-  __atomic_fetch_or(done_mask, bit, __ATOMIC_ACQ_REL);
+  if (cached) __atomic_store_n(&done[dev], 1, __ATOMIC_RELEASE);
   return cudaSuccess;
 }
 
 template <int D>
 cudaError_t launch_for_dim(const LaunchSpec& s) {
   constexpr int smem = static_cast<int>(Cfg<D>::SMEM_BYTES);
-  static unsigned done[4] = {0, 0, 0, 0};
+  static int done[4][kAttrDevices] = {};
   const int v = (s.bf16 ? 1 : 0) | (s.causal ? 2 : 0);
   cudaError_t e;
   switch (v) {
 #define FA_CASE(IDX, BF, CA)                                                       \
   case IDX:                                                                        \
-    e = ensure_smem_attr(fa_fwd_sm100_kernel<D, BF, CA>, smem, &done[IDX]);       \
+    e = ensure_smem_attr(fa_fwd_sm100_kernel<D, BF, CA>, smem, done[IDX]);        \
     if (e != cudaSuccess) return e;                                                \
     fa_fwd_sm100_kernel<D, BF, CA><<<s.grid, kNumThreads, smem, s.stream>>>(s.tq, s.tk, s.tv, s.kp); \
     break;

@@ -2,20 +2,25 @@
 //
 // fa_fwd_sm100 with workspace == NULL allocates its scheduler workspace with
 // cudaMalloc the first time it sees a (device, stream).  Some callers cannot
-// allow that: code running while a CUDA graph is being captured, runtimes that
-// hand out all device memory through their own pool and forbid other
-// allocations, or plug-in hosts that give a library its input and output buffers
-// and nothing else.  This entry point takes its scratch from a fixed array in the
-// library's own device memory instead: every GPU that loads the library holds
-// kScratchBytes of it until the process exits.
+// allow that: runtimes that hand out all device memory through their own pool
+// and forbid allocations behind its back, plug-in hosts that give a library its
+// input and output buffers and nothing else, and latency-bound loops in which the
+// implicit synchronisation of a cudaMalloc is not acceptable.  This entry point
+// takes its scratch from a fixed array in the library's own device memory
+// instead: every GPU that loads the library holds kScratchBytes of it until the
+// process exits.
 //
 // The scratch holds the persistent tile scheduler's counter, which must be zero
-// when a launch starts; fa_fwd_sm100 clears it with cudaMemsetAsync on the
-// caller's stream before every launch, which allocates nothing.  All calls on a
-// device share the one array, so calls whose kernels overlap on the GPU (for
-// example on two streams without ordering between them) race on the counter and
-// compute wrong results: order them, or use fa_fwd_sm100 with one workspace per
-// stream.
+// when a launch starts; it is cleared with cudaMemsetAsync on the caller's stream
+// before every launch, which allocates nothing.  All calls on a device share the
+// one array, so calls whose kernels overlap on the GPU (for example on two
+// streams without ordering between them) race on the counter and compute wrong
+// results: order them, or use fa_fwd_sm100 with one workspace per stream.
+//
+// The array's device address is looked up once per device (the first call on
+// that device, with it current) and cached; a cudaDeviceReset of that device
+// makes the cached address stale, so the entry point must not be called on a
+// device after resetting it in the same process.
 #include <cuda_runtime.h>
 
 #include <cstring>
@@ -74,11 +79,11 @@ int fa_fwd_sm100_noalloc(const fa_fwd_params* p, void* stream) {
     fa::set_last_error("fa_fwd_sm100_noalloc: the scheduler needs more scratch than the static array holds");
     return FA_ERR_BAD_SHAPE;
   }
+  // The device check comes before the symbol lookup, so a device that is not an
+  // sm_100 part is reported as FA_ERR_UNSUPPORTED, as fa_fwd_sm100 reports it.
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) {
-    fa::set_last_error("fa_fwd_sm100_noalloc: no CUDA device");
-    return FA_ERR_UNSUPPORTED;
-  }
+  const int drc = fa::current_sm100_device(&dev, nullptr);
+  if (drc != FA_OK) return drc;
   void* scratch = nullptr;
   const int rc = scratch_address(dev, &scratch);
   if (rc != FA_OK) return rc;

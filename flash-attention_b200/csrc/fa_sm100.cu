@@ -17,6 +17,8 @@
 #include <map>
 #include <mutex>
 #include <string>
+#include <thread>
+#include <tuple>
 #include <utility>
 
 #include "fa_launch.h"
@@ -75,12 +77,27 @@ bool device_info(int dev, DeviceInfo* out) {
   return true;
 }
 
-// Library-owned scheduler workspace, one per (device, stream), allocated on first use.
+// Library-owned scheduler workspace, one per (device, stream), allocated on first
+// use and kept until the process exits (256 bytes each: a process that creates
+// many short-lived streams should pass its own workspace instead).  The handle
+// cudaStreamPerThread names a different stream in every host thread, so for it
+// the calling thread is part of the key: two threads' kernels may overlap and must
+// not share a tile counter.  Like every CUDA allocation, the buffers die with
+// their context: after cudaDeviceReset the cached pointers are stale, so calls
+// with workspace == NULL must not follow a reset of the device in this process.
 void* default_workspace(int dev, cudaStream_t stream) {
+  struct Key {
+    int dev;
+    cudaStream_t stream;
+    std::thread::id thread;
+    bool operator<(const Key& o) const {
+      return std::tie(dev, stream, thread) < std::tie(o.dev, o.stream, o.thread);
+    }
+  };
   static std::mutex mu;
-  static std::map<std::pair<int, cudaStream_t>, void*> cache;
+  static std::map<Key, void*> cache;
+  const Key key{dev, stream, stream == cudaStreamPerThread ? std::this_thread::get_id() : std::thread::id()};
   std::lock_guard<std::mutex> lock(mu);
-  auto key = std::make_pair(dev, stream);
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
   void* p = nullptr;
@@ -184,6 +201,19 @@ int validate_params(const fa_fwd_params* p) {
   Strides st;
   return validate(p, &st);
 }
+
+int current_sm100_device(int* dev_out, int* sms_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(FA_ERR_UNSUPPORTED, "no CUDA device");
+  DeviceInfo di;
+  if (!device_info(dev, &di)) return fail(FA_ERR_LAUNCH, "cudaDeviceGetAttribute failed on device %d", dev);
+  if (di.major != 10 || di.minor != 0)
+    return fail(FA_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a only", dev, di.major,
+                di.minor);
+  *dev_out = dev;
+  if (sms_out) *sms_out = di.sms;
+  return FA_OK;
+}
 }  // namespace fa
 
 extern "C" {
@@ -226,13 +256,9 @@ int fa_fwd_sm100(const fa_fwd_params* p, void* stream_ptr) {
   const int64_t* hs = st.head;
   const int64_t* bs = st.batch;
 
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return fail(FA_ERR_UNSUPPORTED, "no CUDA device");
-  DeviceInfo di;
-  if (!device_info(dev, &di)) return fail(FA_ERR_LAUNCH, "cudaDeviceGetAttribute failed on device %d", dev);
-  if (di.major != 10 || di.minor != 0)
-    return fail(FA_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a only", dev, di.major,
-                di.minor);
+  int dev = 0, sms = 0;
+  const int drc = fa::current_sm100_device(&dev, &sms);
+  if (drc != FA_OK) return drc;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
 
   void* ws = p->workspace;
@@ -262,7 +288,7 @@ int fa_fwd_sm100(const fa_fwd_params* p, void* stream_ptr) {
   kp.heads = h;
   kp.seq_len = n;
   kp.scale_log2 = p->softmax_scale * 1.4426950408889634f;
-  const fa::SchedPlan plan = fa::plan_schedule(b, h, n, fa::kBlockN, di.sms);
+  const fa::SchedPlan plan = fa::plan_schedule(b, h, n, d, fa::kBlockN, sms);
   if (plan.num_tiles < 0)
     return fail(FA_ERR_BAD_SHAPE, "batch*heads*ceil(N/256) = %lld tiles is too many",
                 static_cast<long long>(b) * h * plan.n_pairs);

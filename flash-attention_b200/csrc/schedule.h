@@ -4,10 +4,15 @@
 // (batch, head) slice.  The reference launches one CTA per 64-row query tile,
 // grid (N/64, H, B) (src/forward/forward_v6_mma.cuh:325-412); here persistent CTAs
 // take units from an atomic counter in that order:
-//  * slices are grouped, about one wave of units per group, so the K/V of the
-//    slices in flight stay in L2;
-//  * within a group, units go pair-major: for causal attention the pair with the
-//    most key blocks (the last one) first, so the lightest units end the launch.
+//  * slices are split into groups of equal size whose K and V together stay
+//    under kL2GroupBytes, so the K/V of the slices in flight stay in L2 while
+//    each key block is read by every unit of its slice (at least one wave of
+//    units per group, so small slices still fill the GPU);
+//  * within a group, units go pair-major: for causal attention every slice's
+//    pair with the most key blocks (the last one) first, then the next lighter
+//    pair, so the group runs longest-first and the lightest units end the launch.
+// A CTA claims its next unit only when it reaches that unit's first key block,
+// so the order the counter hands out is the order in which CTAs become free.
 //
 // Plain integer arithmetic, shared by the host (planning, unit tests) and the
 // kernel (decoding).
@@ -18,6 +23,9 @@
 namespace fa {
 
 constexpr int kUnitRows = 256;  // query rows per work unit (two 128-row tiles)
+// K + V bytes of the slices one scheduling group keeps in flight: about half the
+// 126 MB L2, leaving the rest to the streamed Q tiles and O stores.
+constexpr long long kL2GroupBytes = 64ll << 20;
 
 struct SchedPlan {
   int n_pairs;    // ceil(N / 256): units per slice
@@ -27,17 +35,25 @@ struct SchedPlan {
   int grid;       // persistent CTAs: min(num_tiles, sms)
 };
 
-// Host plan for B x H slices of N rows on a GPU with `sms` SMs.
-FA_HD SchedPlan plan_schedule(int batch, int heads, int seq_len, int key_block, int sms) {
+// Host plan for B x H slices of N rows of head_dim 16-bit elements on a GPU with
+// `sms` SMs.
+FA_HD SchedPlan plan_schedule(int batch, int heads, int seq_len, int head_dim, int key_block, int sms) {
   SchedPlan s;
   s.n_pairs = (seq_len + kUnitRows - 1) / kUnitRows;
   s.n_kv = (seq_len + key_block - 1) / key_block;
-  const long long tiles = static_cast<long long>(batch) * heads * s.n_pairs;
+  const long long bh = static_cast<long long>(batch) * heads;
+  const long long tiles = bh * s.n_pairs;
   s.num_tiles = tiles > (1ll << 30) ? -1 : static_cast<int>(tiles);  // -1: too many
-  int g = (sms + s.n_pairs - 1) / s.n_pairs;
+  // Fewest groups whose K + V fit the budget, then slices spread evenly over them.
+  const long long kv_bytes = 4ll * seq_len * head_dim;  // K and V of one slice
+  long long groups = (bh * kv_bytes + kL2GroupBytes - 1) / kL2GroupBytes;
+  if (groups < 1) groups = 1;
+  long long g = (bh + groups - 1) / groups;
+  const long long wave = (sms + s.n_pairs - 1) / s.n_pairs;  // slices that give one unit per SM
+  if (g < wave) g = wave;
+  if (g > bh) g = bh;
   if (g < 1) g = 1;
-  if (g > batch * heads) g = batch * heads;
-  s.group_bh = g;
+  s.group_bh = static_cast<int>(g);
   s.grid = static_cast<int>(tiles < sms ? tiles : sms);
   return s;
 }

@@ -11,11 +11,18 @@ Draw order per configuration: Q, then K, then V with ``torch.randn`` in fp32;
 for the outlier sweep the same generator then draws ``rand < 0.01`` masks for
 Q and then K and multiplies the selected entries by 20; finally all three are
 rounded to the configuration's dtype.
+
+``generate_qkv`` is the reference callers' own generator interface
+(benchmark/python/input_data.py:115-145): the same keyword arguments, draws on
+the given device in the given dtype, and a per-case seed ``seed + 100003 *
+case_index`` (input_data.py:11-12), so the reference's correctness gate and
+benchmark loop run unchanged against this module.
 """
 from __future__ import annotations
 
 import math
 from dataclasses import dataclass
+from pathlib import Path
 from typing import Optional
 
 import torch
@@ -124,3 +131,88 @@ def make_stress(shape, dtype, seed: int):
     k = k - km.to(torch.float32) * 256.0
     v = v + vm.to(torch.float32) * 64.0
     return q.to(dtype).contiguous(), k.to(dtype).contiguous(), v.to(dtype).contiguous()
+
+
+# ---------------------------------------------------------------------------
+# The reference callers' generator (benchmark/python/input_data.py), drawn on a
+# device.  Same modes and argument names; the formulas are the ones above.
+
+_CASE_SEED_STRIDE = 100_003  # input_data.py:11-12
+
+
+def case_seed(seed: int, case_index: int) -> int:
+    """Seed of case `case_index` of a run with base seed `seed`."""
+    return int(seed + case_index * _CASE_SEED_STRIDE)
+
+
+def _device_gen(seed: int, device) -> torch.Generator:
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    return g
+
+
+def _draw_random(shape, dtype, device, seed):
+    g = _device_gen(seed, device)
+    return tuple(torch.randn(shape, device=device, dtype=dtype, generator=g).contiguous() for _ in range(3))
+
+
+def _draw_stress(shape, dtype, device, seed):
+    g = _device_gen(seed, device)
+    base = [torch.randn(shape, device=device, dtype=torch.float32, generator=g) * s for s in (32.0, 32.0, 16.0)]
+    masks = [torch.rand(shape, device=device, generator=g) < 0.001 for _ in range(3)]
+    q = base[0] + masks[0].to(torch.float32) * 256.0
+    k = base[1] - masks[1].to(torch.float32) * 256.0
+    v = base[2] + masks[2].to(torch.float32) * 64.0
+    return tuple(t.to(dtype=dtype).contiguous() for t in (q, k, v))
+
+
+def _load_replay(shape, dtype, device, replay_dir, replay_file):
+    """q, k, v from a saved .pt (dict with q/k/v, or a 3-sequence); [B, N, H, d]
+    tensors are permuted to [B, H, N, d] (input_data.py:65-112)."""
+    replay_dir = Path(replay_dir) if replay_dir is not None else Path(".")
+    if replay_file:
+        path = Path(replay_file).expanduser()
+        if not path.is_absolute():
+            path = replay_dir / path
+        if not path.exists():
+            raise RuntimeError(f"Replay file not found: {path}")
+    else:
+        found = sorted(replay_dir.glob("*.pt"))
+        if not found:
+            raise RuntimeError(f"Replay mode selected but no .pt file found in: {replay_dir}")
+        path = found[0]
+    obj = torch.load(path, map_location="cpu")
+    if isinstance(obj, dict) and all(key in obj for key in ("q", "k", "v")):
+        tensors = (obj["q"], obj["k"], obj["v"])
+    elif isinstance(obj, (list, tuple)) and len(obj) >= 3:
+        tensors = tuple(obj[:3])
+    else:
+        raise RuntimeError("Replay file must be a dict(q,k,v) or tuple/list(q,k,v)")
+    b, h, n, d = shape
+    out = []
+    for t in tensors:
+        if tuple(t.shape) == (b, n, h, d) and (b, n, h, d) != tuple(shape):
+            t = t.permute(0, 2, 1, 3)
+        elif tuple(t.shape) != tuple(shape):
+            raise RuntimeError(f"Replay tensor shape {tuple(t.shape)} does not match {tuple(shape)} or [B,N,H,D]")
+        out.append(t.to(device=device, dtype=dtype).contiguous())
+    return out[0], out[1], out[2], path
+
+
+def generate_qkv(*, batch_size: int, n_heads: int, seq_len: int, d_head: int, dtype: torch.dtype, device,
+                 input_mode: str, seed: int, case_index: int, replay_dir=None, replay_file: str = ""):
+    """(q, k, v, replay_path) for one case of the reference's benchmark/correctness
+    drivers: ``random``, ``structured``, ``stress`` or ``replay`` inputs of shape
+    [batch_size, n_heads, seq_len, d_head] in `dtype` on `device`."""
+    shape = (batch_size, n_heads, seq_len, d_head)
+    seeded = case_seed(seed, case_index)
+    if input_mode == "random":
+        return (*_draw_random(shape, dtype, device, seeded), None)
+    if input_mode == "structured":
+        q, k, v = make_structured(shape, dtype)
+        return q.to(device), k.to(device), v.to(device), None
+    if input_mode == "stress":
+        return (*_draw_stress(shape, dtype, device, seeded), None)
+    if input_mode == "replay":
+        return _load_replay(shape, dtype, device, replay_dir, replay_file)
+    raise RuntimeError(f"Unsupported input_mode: {input_mode}")

@@ -81,8 +81,9 @@ typedef struct fa_fwd_params {
   int64_t stride_head64[4];
   /* Scratch for the persistent tile scheduler: at least fa_fwd_workspace_bytes(),
    * 16-byte aligned device memory, or NULL to let the library use a buffer it
-   * allocates once per (device, stream).  Launches that overlap on the GPU must
-   * not share a workspace. */
+   * allocates once per (device, stream) - per host thread for
+   * cudaStreamPerThread - and keeps until exit.  Launches that overlap on the
+   * GPU must not share a workspace. */
   void* workspace;
   size_t workspace_bytes;
   int* status;                 /* optional device int: set to 0x100|site if a wait times out */
@@ -94,15 +95,18 @@ typedef struct fa_fwd_params {
 FA_API int fa_fwd_sm100(const fa_fwd_params* params, void* stream);
 
 /* Same computation as fa_fwd_sm100, for callers that cannot allocate device
- * memory (code running during CUDA-graph capture, runtimes whose memory pool
- * forbids outside allocations, plug-in hosts that pass only input and output
- * buffers).  No counterpart in the reference.  params->workspace must be NULL:
- * the scheduler's scratch is a fixed 256-byte array inside this library's device
+ * memory: runtimes whose memory pool forbids allocations behind its back,
+ * plug-in hosts that hand a library only its input and output buffers, and
+ * latency-bound loops that cannot take a cudaMalloc's implicit synchronisation.
+ * No counterpart in the reference.  params->workspace must be NULL: the
+ * scheduler's scratch is a fixed 256-byte array inside this library's device
  * memory (one per GPU, held until the process exits), cleared with
- * cudaMemsetAsync before every launch.  No cudaMalloc / cudaFree is called.  The
+ * cudaMemsetAsync before every launch; a scheduler needing more than 256 bytes
+ * is rejected with FA_ERR_BAD_SHAPE.  No cudaMalloc / cudaFree is called.  The
  * first call on a device looks up the array's address (cudaGetSymbolAddress)
- * and must therefore come before any stream capture.  All calls on a device
- * share the array: calls whose kernels overlap on the GPU race on it. */
+ * with that device current, and must therefore come before any stream capture;
+ * after a cudaDeviceReset of that device the cached address is stale.  All calls
+ * on a device share the array: calls whose kernels overlap on the GPU race on it. */
 FA_API int fa_fwd_sm100_noalloc(const fa_fwd_params* params, void* stream);
 
 /* Dynamic shared memory one CTA of the kernel uses for this head_dim / dtype

@@ -66,3 +66,55 @@ def test_l2_flush_policy():
     assert not bench.needs_flush(CONFIGS["cfg2"], 8, "weak")
     assert bench.rank_bytes(CONFIGS["cfg2"], 1, "weak") == 4 * 8 * 32 * 4096 * 128 * 2
     assert "no flush" in bench.l2_note(CONFIGS["cfg2"], 1, "weak")
+
+
+def test_strong_split_is_the_default_and_checked_slices_are_strided():
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    from flash_attention_runtime.inputs import CONFIGS
+
+    args = bench.parse_args([])
+    assert args.scaling == "strong" and args.gpus == 1 and args.warmup >= 3
+    assert bench.check_slices(256, 8) == [0, 36, 73, 109, 146, 182, 219, 255]
+    assert bench.check_slices(4, 8) == [0, 1, 2, 3]
+    assert bench.check_slices(64, 0) == []
+    c = bench.workload_config(CONFIGS["cfg2"], 8, "strong")
+    assert c["slices"] == 256 and c["slices_per_rank"] == 32 and c["global_batch"] == 8
+    c = bench.workload_config(CONFIGS["cfg2"], 8, "weak")
+    assert c["slices"] == 8 * 256 and c["slices_per_rank"] == 256 and c["batch_per_rank"] == 8
+
+
+def test_peak_follows_the_timed_region_length():
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    peaks = {"bf16_tflops": 1663.7, "bf16_tflops_sustained": 1389.2}
+    assert bench.pick_peak(peaks, 0.02) == (1663.7, "bf16_tflops")
+    assert bench.pick_peak(peaks, 1.5) == (1389.2, "bf16_tflops_sustained")
+
+
+def test_verify_accepts_the_exact_result_and_rejects_a_planted_error():
+    """The gathered-output check on CPU tensors: the float64 result rounded to the
+    output dtype passes; the same with one element moved by 2e-2 fails."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    from flash_attention_runtime.inputs import AttnConfig, generate
+
+    cfg = AttnConfig("tiny", 1, 3, 96, 32, torch.bfloat16, True, 5)
+    q, k, v = generate(cfg)
+    outs, lses = [], []
+    for i in range(cfg.slices):
+        o, l = bench.reference_slice(q[0, i], k[0, i], v[0, i], cfg.scale, cfg.causal)
+        outs.append(o.to(torch.bfloat16))
+        lses.append(l.float())
+    o_all, l_all = torch.stack(outs), torch.stack(lses)
+    r = bench.verify(cfg, (q, k, v), o_all, l_all, [0, 1, 2], torch.device("cpu"))
+    assert r["ok"] and r["all_finite"] and r["max_abs_vs_ref_rounded_to_dtype"] == 0.0
+    bad = o_all.clone()
+    bad[1, 50, 7] += 2e-2
+    r = bench.verify(cfg, (q, k, v), bad, l_all, [0, 1, 2], torch.device("cpu"))
+    assert not r["ok"]
+    r = bench.verify(cfg, (q, k, v), o_all, l_all + 1e-3, [0, 2], torch.device("cpu"))
+    assert not r["ok"]
