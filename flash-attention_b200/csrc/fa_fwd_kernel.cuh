@@ -69,7 +69,8 @@ struct KernelParams {
   int n_kv;          // ceil(N / 128): key/value blocks per slice
   int num_tiles;     // batch * heads * n_pairs
   int group_bh;      // slices per scheduling group
-  int* tile_counter; // workspace word, zero at launch
+  int* tile_counter; // workspace words: [0] unit counter, [1] finished CTAs; both zero at
+                    // launch, and the last CTA to finish sets both back to zero
   int* status;       // optional device status word (may be null)
   unsigned long long timeout_ns;
 };
@@ -364,6 +365,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+  // Everything above touches only this CTA's shared memory and TMEM; with a
+  // programmatic launch the previous kernel on the stream may still be running
+  // (and writing Q, K, V, O, LSE or the workspace) until this returns.
+  grid_dependency_wait();
 
   if (warp >= kProducerWarp) {
     setmaxnreg_dec<80>();
@@ -445,6 +450,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           ok = publish(next);
           if (!ok) break;
           if (!has_next) {
+            // No more units for this CTA: a dependent launch may take the SM as
+            // soon as it exits.
+            grid_launch_dependents();
             ok = load_pair(nmax - 1, t, -1, t);
             break;
           }
@@ -793,6 +801,18 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+  if (threadIdx.x == 0) {
+    // Every unit claim of this CTA (its producer's atomics, whose results it
+    // used) is complete; the CTA that finishes last knows all CTAs' claims are,
+    // and leaves the workspace zeroed for the next launch on the stream.
+    __threadfence();
+    unsigned* done = reinterpret_cast<unsigned*>(p.tile_counter + 1);
+    if (atomicAdd(done, 1u) == gridDim.x - 1) {
+      __threadfence();
+      atomicExch(p.tile_counter, 0);
+      atomicExch(reinterpret_cast<int*>(done), 0);
+    }
   }
 }
 

@@ -56,13 +56,27 @@ cudaError_t launch_for_dim(const LaunchSpec& s) {
   constexpr int smem = static_cast<int>(Cfg<D>::SMEM_BYTES);
   static int done[4][kAttrDevices] = {};
   const int v = (s.bf16 ? 1 : 0) | (s.causal ? 2 : 0);
+  // Programmatic dependent launch: this grid's CTAs may start (barrier setup,
+  // TMEM allocation) while the previous kernel on the stream finishes; they wait
+  // in griddepcontrol.wait for it to complete before touching global memory.
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(s.grid));
+  cfg.blockDim = dim3(kNumThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s.stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   cudaError_t e;
   switch (v) {
 #define FA_CASE(IDX, BF, CA)                                                       \
   case IDX:                                                                        \
     e = ensure_smem_attr(fa_fwd_sm100_kernel<D, BF, CA>, smem, done[IDX]);        \
     if (e != cudaSuccess) return e;                                                \
-    fa_fwd_sm100_kernel<D, BF, CA><<<s.grid, kNumThreads, smem, s.stream>>>(s.tq, s.tk, s.tv, s.kp); \
+    e = cudaLaunchKernelEx(&cfg, fa_fwd_sm100_kernel<D, BF, CA>, s.tq, s.tk, s.tv, s.kp); \
+    if (e != cudaSuccess) return e;                                                \
     break;
     FA_CASE(0, false, false)
     FA_CASE(1, true, false)

@@ -102,6 +102,11 @@ void* default_workspace(int dev, cudaStream_t stream) {
   if (it != cache.end()) return it->second;
   void* p = nullptr;
   if (cudaMalloc(&p, fa_fwd_workspace_bytes()) != cudaSuccess) return nullptr;
+  // Zeroed once; every launch leaves it zeroed again (its last CTA resets it).
+  if (cudaMemset(p, 0, fa_fwd_workspace_bytes()) != cudaSuccess) {
+    cudaFree(p);
+    return nullptr;
+  }
   cache[key] = p;
   return p;
 }
@@ -262,7 +267,8 @@ int fa_fwd_sm100(const fa_fwd_params* p, void* stream_ptr) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
 
   void* ws = p->workspace;
-  if (ws) {
+  const bool caller_ws = ws != nullptr;
+  if (caller_ws) {
     if (p->workspace_bytes < fa_fwd_workspace_bytes() || !aligned16(ws))
       return fail(FA_ERR_BAD_PARAM, "workspace must be >= %zu bytes and 16-byte aligned", fa_fwd_workspace_bytes());
   } else {
@@ -304,8 +310,14 @@ int fa_fwd_sm100(const fa_fwd_params* p, void* stream_ptr) {
   s.bf16 = bf16;
   s.causal = p->causal != 0;
 
-  cudaError_t e = cudaMemsetAsync(ws, 0, sizeof(int), stream);
-  if (e != cudaSuccess) return fail(FA_ERR_LAUNCH, "cudaMemsetAsync(workspace): %s", cudaGetErrorString(e));
+  // The scheduler's two counter words start at zero.  A library-owned workspace
+  // is zeroed at allocation and every launch leaves it zeroed; a caller's
+  // workspace is cleared here, on the caller's stream, as the interface promises.
+  cudaError_t e = cudaSuccess;
+  if (caller_ws) {
+    e = cudaMemsetAsync(ws, 0, 2 * sizeof(int), stream);
+    if (e != cudaSuccess) return fail(FA_ERR_LAUNCH, "cudaMemsetAsync(workspace): %s", cudaGetErrorString(e));
+  }
   switch (d) {
     case 32: e = fa::launch_d32(s); break;
     case 64: e = fa::launch_d64(s); break;

@@ -217,6 +217,14 @@ __device__ __forceinline__ float2 add2(float2 a, float2 b) {
 
 // ---------------------------------------------------------------- misc
 
+// Programmatic dependent launch.  wait: block until the grids this one depends on
+// have completed and their memory is visible.  launch_dependents: this CTA needs
+// no more SM resources for new work, so dependent grids may start launching.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

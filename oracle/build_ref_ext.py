@@ -10,7 +10,7 @@ rest of oracle/_ref).  Only `bench.py --impl reference --ref-device gpu` loads
 it, to time the reference kernel on the shapes it supports: fp16, d = 128,
 non-causal, N % 64 == 0.  Nothing in the product path uses it.
 
-Usage: python oracle/build_ref_ext.py [reference_root]
+Usage: python oracle/build_ref_ext.py <reference_root>   (or FA_REFERENCE_ROOT in the environment)
 """
 from __future__ import annotations
 
@@ -28,7 +28,12 @@ def built_module_path() -> Path:
 
 
 def main(argv: list[str]) -> int:
-    ref = Path(argv[1]) if len(argv) > 1 else Path(os.environ.get("FA_REFERENCE_ROOT", "/root/reference"))
+    root = argv[1] if len(argv) > 1 else os.environ.get("FA_REFERENCE_ROOT", "")
+    if not root:
+        print("usage: build_ref_ext.py <reference_root> (or set FA_REFERENCE_ROOT); "
+              f"keeping any prebuilt {built_module_path()}")
+        return 0
+    ref = Path(root)
     src = ref / "python" / "flash_attention_runtime" / "_ext.cu"
     if not src.exists():
         print(f"reference source {src} not found; keeping any prebuilt {built_module_path()}")

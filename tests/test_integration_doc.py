@@ -1,7 +1,7 @@
-"""The binding examples in INTEGRATION.md stay in step with the header and the
-library: the C++ driver snippet compiles against include/fa_sm100.h, and the
-ctypes stub runs against libfa_sm100.so (here without a GPU, so the call must
-return an error with a message instead of launching)."""
+"""Doc test: the binding examples of the repository's integration guide stay in
+step with the header and the library.  The C++ driver snippet compiles against
+include/fa_sm100.h, and the ctypes stub runs against libfa_sm100.so (here without
+a GPU, so the call must return an error with a message instead of launching)."""
 from __future__ import annotations
 
 import ctypes
@@ -53,7 +53,7 @@ def test_ctypes_stub_runs_and_reports_errors():
     os.chdir(ROOT)
     try:
         with pytest.raises(RuntimeError) as e:
-            exec(compile(stub, "INTEGRATION.md#3", "exec"), env)  # noqa: S102
+            exec(compile(stub, "integration-guide-ctypes-stub", "exec"), env)  # noqa: S102
     finally:
         os.chdir(cwd)
     assert str(e.value)  # the library's own message, e.g. that no CUDA device is present

@@ -1,6 +1,7 @@
 """GPU test of fa_fwd_sm100_noalloc, the entry point for callers that cannot
-allocate device memory (graph capture, pool-only runtimes, plug-in hosts that
-only hand over input and output buffers).
+allocate device memory: runtimes whose memory pool forbids allocations behind its
+back, plug-in hosts that hand a library only its input and output buffers, and
+latency-bound loops that cannot take a cudaMalloc's implicit synchronisation.
 
 It runs the same computation as fa_fwd_sm100 but keeps the scheduler's scratch
 in a fixed array inside the library instead of a cudaMalloc'd workspace.  The
@@ -10,11 +11,6 @@ on two calls in a row (the second call checks that the shared scratch is cleared
 between launches).  This file is collected last, and it also passes when run
 alone in a fresh process, where its first call is the one that looks up the
 scratch address.
-
-A third test captures the entry point in a CUDA graph (torch's default, global
-capture mode, which fails any call that could allocate or synchronise) and
-replays the graph on new inputs copied into the captured buffers, checking each
-replay against the CPU oracle.
 """
 from __future__ import annotations
 
@@ -24,7 +20,6 @@ import math
 import pytest
 import torch
 
-from oracle.oracle import oracle_attention
 from parity import compare_lse, compare_output
 
 from flash_attention_runtime import _lib
@@ -87,59 +82,6 @@ def test_noalloc_entry_point_matches_default(shape, dtype, causal):
         rl = compare_lse(lse, lse_ref.cpu().numpy())
         assert ro["ok"], ro
         assert rl["ok"], rl
-
-
-@pytest.mark.parametrize("shape,dtype,causal", [
-    ((1, 3, 700, 128), torch.bfloat16, True),
-    ((2, 2, 512, 64), torch.float16, False),
-])
-def test_noalloc_entry_point_in_a_cuda_graph(shape, dtype, causal):
-    lib = _lib.load()
-    lib.fa_fwd_sm100_noalloc.argtypes = [ctypes.POINTER(_lib.FwdParams), ctypes.c_void_p]
-    lib.fa_fwd_sm100_noalloc.restype = ctypes.c_int
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    scale = 1.0 / math.sqrt(shape[-1])
-    q, k, v = (torch.empty(shape, dtype=dtype, device=dev) for _ in range(3))
-    o = torch.empty_like(q)
-    lse = torch.empty(shape[:3], dtype=torch.float32, device=dev)
-    status = torch.zeros(1, dtype=torch.int32, device=dev)
-    p = _params(q, k, v, o, lse, scale, causal, status)
-
-    # One call outside capture on the capture stream: it resolves the scratch
-    # address and sets the kernel's shared-memory attribute, neither of which
-    # is a stream operation.
-    side = torch.cuda.Stream(dev)
-    side.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(side):
-        for t in (q, k, v):
-            t.normal_()
-        assert lib.fa_fwd_sm100_noalloc(ctypes.byref(p), ctypes.c_void_p(side.cuda_stream)) == _lib.FA_OK, \
-            lib.fa_last_error()
-    torch.cuda.current_stream(dev).wait_stream(side)
-    torch.cuda.synchronize(dev)
-
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        s = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
-        rc = lib.fa_fwd_sm100_noalloc(ctypes.byref(p), s)
-    assert rc == _lib.FA_OK, lib.fa_last_error()
-
-    for seed in (5, 6):
-        qh, kh, vh = make_random(shape, dtype, seed=seed)
-        for dst, src in ((q, qh), (k, kh), (v, vh)):
-            dst.copy_(src)
-        o.fill_(float("nan"))
-        lse.fill_(float("nan"))
-        g.replay()
-        torch.cuda.synchronize(dev)
-        assert int(status.item()) == 0
-        ref_o, ref_lse = oracle_attention(qh.float().numpy(), kh.float().numpy(), vh.float().numpy(), scale, causal)
-        ro = compare_output(o, ref_o, dtype)
-        rl = compare_lse(lse, ref_lse)
-        assert ro["ok"], ro
-        assert rl["ok"], rl
-    del g
 
 
 def test_noalloc_rejects_a_workspace():
