@@ -41,7 +41,7 @@ def test_reference_arm_prints_one_contract_line():
     assert 1 <= cb["cores"] <= 4  # cfg0 has 4 (b,h) slices: no more threads than slices
     assert cb["sample"].startswith(f"{cb['cores']} of the 4 (b,h) slices of cfg0")
     assert d["e2e"] == {"value": d["value"], "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
-    assert "flushed" in d["config"]["l2"]
+    assert "rotating" in d["config"]["l2"]
 
 
 def test_our_arm_fails_loudly_without_a_gpu():
@@ -52,20 +52,25 @@ def test_our_arm_fails_loudly_without_a_gpu():
     assert r.stdout.strip() == ""
 
 
-def test_l2_flush_policy():
+def test_l2_policy_rotates_input_copies_for_small_ranks():
     sys.path.insert(0, str(ROOT))
     import bench
 
     from flash_attention_runtime.inputs import CONFIGS
 
-    flushed = {name for name, cfg in CONFIGS.items() if bench.needs_flush(cfg, 1, "weak")}
-    assert {"cfg0", "cfg1", "cfg4_d32"} <= flushed
-    assert not flushed & {"cfg2", "cfg3", "cfg4_d128"}
-    # Strong scaling splits the slices: at 8 ranks configuration 2 is 134 MB per rank.
-    assert bench.needs_flush(CONFIGS["cfg2"], 8, "strong")
-    assert not bench.needs_flush(CONFIGS["cfg2"], 8, "weak")
+    rotated = {name for name, cfg in CONFIGS.items() if bench.input_copies(cfg, 1, "strong") > 1}
+    assert {"cfg0", "cfg1", "cfg4_d32"} <= rotated
+    assert not rotated & {"cfg2", "cfg3", "cfg4_d128"}
+    # Strong scaling splits the slices: at 8 ranks configuration 2 is 134 MB per rank,
+    # so three copies rotate (two launches, 268 MB, between uses of one copy).
+    assert bench.input_copies(CONFIGS["cfg2"], 8, "strong") == 3
+    assert bench.input_copies(CONFIGS["cfg2"], 8, "weak") == 1
+    for name, cfg in CONFIGS.items():
+        n = bench.input_copies(cfg, 1, "strong")
+        assert n == 1 or (n - 1) * bench.rank_bytes(cfg, 1, "strong") >= 2 * bench.L2_BYTES
     assert bench.rank_bytes(CONFIGS["cfg2"], 1, "weak") == 4 * 8 * 32 * 4096 * 128 * 2
-    assert "no flush" in bench.l2_note(CONFIGS["cfg2"], 1, "weak")
+    assert "inputs larger than L2" in bench.l2_note(CONFIGS["cfg2"], 1, "weak")
+    assert "rotating over 3 copies" in bench.l2_note(CONFIGS["cfg2"], 8, "strong")
 
 
 def test_strong_split_is_the_default_and_checked_slices_are_strided():
