@@ -71,6 +71,9 @@ def parse_args(argv=None):
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--verify-slices", type=int, default=8,
                     help="slices of the gathered output checked against float64 (0: no check)")
+    ap.add_argument("--share-of", type=int, default=1,
+                    help="on one GPU without torchrun: time rank 0's share of an N-way strong split "
+                         "(to profile one rank's launch)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-device", choices=["cpu", "gpu"], default="cpu",
                     help="with --impl reference: gpu times the reference's own CUDA kernel instead "
@@ -371,8 +374,8 @@ def half_ulp(x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
 
 def verify(cfg: AttnConfig, full, o_all: torch.Tensor, lse_all: torch.Tensor, slices, dev):
     """Check `slices` of the gathered O / LSE ([S, N, d] / [S, N]) against float64."""
-    q, k, v = full  # [B, H, N, d] on the CPU
-    flat = lambda t: t.reshape(cfg.slices, cfg.seq_len, cfg.head_dim)  # noqa: E731
+    q, k, v = full  # the slices behind o_all, [B, H, N, d] or [S, N, d], on the CPU
+    flat = lambda t: t.reshape(-1, cfg.seq_len, cfg.head_dim)  # noqa: E731
     qf, kf, vf = flat(q), flat(k), flat(v)
     atol = ATOL[cfg.dtype]
     max_abs = max_rounded = lse_rel = worst_excess = 0.0
@@ -437,9 +440,12 @@ def run_ours(args, cfg: AttnConfig):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    (qh, kh, vh), full, first_slice = rank_inputs(cfg, rank, world, args.scaling)
+    # --share-of N on a single process stands in for rank 0 of an N-way strong split
+    share = args.share_of if (world == 1 and args.scaling == "strong" and args.share_of > 1) else 1
+    split_world = world * share
+    (qh, kh, vh), full, first_slice = rank_inputs(cfg, rank, split_world, args.scaling)
     n_slices = qh.shape[0] * qh.shape[1]
-    n_copies = input_copies(cfg, world, args.scaling)
+    n_copies = input_copies(cfg, split_world, args.scaling)
     copies = []
     for _ in range(n_copies):
         q, k, v = qh.to(dev), kh.to(dev), vh.to(dev)
@@ -489,7 +495,7 @@ def run_ours(args, cfg: AttnConfig):
     ms_per_step = max_over_ranks(total_ms / args.steps)
     launch_ms_max = max_over_ranks(launch_ms)
     flops_rank = cfg.flops(n_slices)
-    total_flops = flops_rank * world if args.scaling == "weak" else cfg.flops()
+    total_flops = flops_rank * world if args.scaling == "weak" else cfg.flops() / share
     value = total_flops / (ms_per_step * 1e-3) / 1e12
     timed_region_s = ms_per_step * args.steps / 1e3
 
@@ -500,7 +506,10 @@ def run_ours(args, cfg: AttnConfig):
         s_total = cfg.slices  # strong: the whole configuration; weak: rank 0's own batch
         o_loc = o.reshape(1, n_slices, cfg.seq_len, cfg.head_dim)
         l_loc = lse.reshape(1, n_slices, cfg.seq_len)
-        if args.scaling == "strong" and world > 1:
+        if share > 1:
+            o_all, l_all = o_loc[0], l_loc[0]
+            gathered = f"local (rank 0's share of a {share}-way split)"
+        elif args.scaling == "strong" and world > 1:
             o_all = gather(o_loc, s_total)
             l_all = gather(l_loc, s_total)
             gathered = f"NCCL all_gather of O and LSE over {world} ranks"
@@ -509,6 +518,11 @@ def run_ours(args, cfg: AttnConfig):
             gathered = "local (one rank holds every slice)" if world == 1 else "local (weak scaling, rank 0's batch)"
         torch.cuda.synchronize(dev)
         if rank == 0:
+            if share > 1:
+                s_total = n_slices
+                q_, k_, v_ = full
+                cut = lambda t: t.reshape(cfg.slices, cfg.seq_len, cfg.head_dim)[:n_slices]  # noqa: E731
+                full = (cut(q_), cut(k_), cut(v_))
             parity = verify(cfg, full, o_all, l_all, check_slices(s_total, args.verify_slices), dev)
             parity["gathered"] = gathered
         del o_all, l_all
@@ -620,7 +634,7 @@ def run_ours(args, cfg: AttnConfig):
             "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
             "dtype": "bf16" if cfg.dtype == torch.bfloat16 else "f16",
             "data": "synthetic (seeded N(0,1), generated on CPU)",
-            "config": workload_config(cfg, world, args.scaling),
+            "config": {**workload_config(cfg, split_world, args.scaling), **({"share_of": share} if share > 1 else {})},
             "parity": parity,
             "e2e": {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms, "steps": e2e_steps, "chunks": n_chunks,
