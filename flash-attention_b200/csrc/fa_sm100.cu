@@ -294,7 +294,7 @@ int fa_fwd_sm100(const fa_fwd_params* p, void* stream_ptr) {
   kp.heads = h;
   kp.seq_len = n;
   kp.scale_log2 = p->softmax_scale * 1.4426950408889634f;
-  const fa::SchedPlan plan = fa::plan_schedule(b, h, n, d, fa::kBlockN, sms);
+  const fa::SchedPlan plan = fa::plan_schedule(b, h, n, d, fa::kBlockN, sms, p->causal != 0);
   if (plan.num_tiles < 0)
     return fail(FA_ERR_BAD_SHAPE, "batch*heads*ceil(N/256) = %lld tiles is too many",
                 static_cast<long long>(b) * h * plan.n_pairs);

@@ -4,10 +4,13 @@
 // (batch, head) slice.  The reference launches one CTA per 64-row query tile,
 // grid (N/64, H, B) (src/forward/forward_v6_mma.cuh:325-412); here persistent CTAs
 // take units from an atomic counter in that order:
-//  * slices are split into groups of equal size whose K and V together stay
-//    under kL2GroupBytes, so the K/V of the slices in flight stay in L2 while
-//    each key block is read by every unit of its slice (at least one wave of
-//    units per group, so small slices still fill the GPU);
+//  * slices are grouped so that the K/V of the slices in flight stay in L2 while
+//    each key block is read by every unit of its slice.  Without a causal mask
+//    all units cost the same and a group is one wave of units (about one unit
+//    per SM, all reading the same slices' K/V at the same time).  With a causal
+//    mask a group is as many slices as fit kL2GroupBytes of K and V, split into
+//    groups of equal size (at least one wave each), so that the longest-first
+//    order below has many units to balance;
 //  * within a group, units go pair-major: for causal attention every slice's
 //    pair with the most key blocks (the last one) first, then the next lighter
 //    pair, so the group runs longest-first and the lightest units end the launch.
@@ -37,20 +40,23 @@ struct SchedPlan {
 
 // Host plan for B x H slices of N rows of head_dim 16-bit elements on a GPU with
 // `sms` SMs.
-FA_HD SchedPlan plan_schedule(int batch, int heads, int seq_len, int head_dim, int key_block, int sms) {
+FA_HD SchedPlan plan_schedule(int batch, int heads, int seq_len, int head_dim, int key_block, int sms, bool causal) {
   SchedPlan s;
   s.n_pairs = (seq_len + kUnitRows - 1) / kUnitRows;
   s.n_kv = (seq_len + key_block - 1) / key_block;
   const long long bh = static_cast<long long>(batch) * heads;
   const long long tiles = bh * s.n_pairs;
   s.num_tiles = tiles > (1ll << 30) ? -1 : static_cast<int>(tiles);  // -1: too many
-  // Fewest groups whose K + V fit the budget, then slices spread evenly over them.
-  const long long kv_bytes = 4ll * seq_len * head_dim;  // K and V of one slice
-  long long groups = (bh * kv_bytes + kL2GroupBytes - 1) / kL2GroupBytes;
-  if (groups < 1) groups = 1;
-  long long g = (bh + groups - 1) / groups;
   const long long wave = (sms + s.n_pairs - 1) / s.n_pairs;  // slices that give one unit per SM
-  if (g < wave) g = wave;
+  long long g = wave;
+  if (causal) {
+    // Fewest groups whose K + V fit the budget, then slices spread evenly over them.
+    const long long kv_bytes = 4ll * seq_len * head_dim;  // K and V of one slice
+    long long groups = (bh * kv_bytes + kL2GroupBytes - 1) / kL2GroupBytes;
+    if (groups < 1) groups = 1;
+    g = (bh + groups - 1) / groups;
+    if (g < wave) g = wave;
+  }
   if (g > bh) g = bh;
   if (g < 1) g = 1;
   s.group_bh = static_cast<int>(g);

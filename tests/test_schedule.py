@@ -35,8 +35,8 @@ def sched(tmp_path_factory):
     src.write_text(
         '#include "schedule.h"\n'
         'extern "C" {\n'
-        "fa::SchedPlan s_plan(int b, int h, int n, int d, int kb, int sms)"
-        " { return fa::plan_schedule(b, h, n, d, kb, sms); }\n"
+        "fa::SchedPlan s_plan(int b, int h, int n, int d, int kb, int sms, int causal)"
+        " { return fa::plan_schedule(b, h, n, d, kb, sms, causal != 0); }\n"
         "fa::TileInfo s_decode(int t, int b, int h, int n, int np, int nkv, int g, int kb, int causal)"
         " { return fa::decode_unit(t, b, h, n, np, nkv, g, kb, causal != 0); }\n"
         "}\n")
@@ -44,7 +44,7 @@ def sched(tmp_path_factory):
     subprocess.run(["g++", "-O1", "-std=c++17", "-shared", "-fPIC", f"-I{CSRC}", str(src), "-o", str(so)], check=True)
     lib = ctypes.CDLL(str(so))
     lib.s_plan.restype = Plan
-    lib.s_plan.argtypes = [ctypes.c_int] * 6
+    lib.s_plan.argtypes = [ctypes.c_int] * 7
     lib.s_decode.restype = Tile
     lib.s_decode.argtypes = [ctypes.c_int] * 9
     return lib
@@ -62,7 +62,7 @@ def _cdiv(a, b):
 @pytest.mark.parametrize("causal", [False, True])
 def test_units_cover_every_slice_pair_once(sched, b, h, n, causal):
     sms = 148
-    p = sched.s_plan(b, h, n, 128, KEY_BLOCK, sms)
+    p = sched.s_plan(b, h, n, 128, KEY_BLOCK, sms, int(causal))
     assert p.n_pairs == _cdiv(n, 256) and p.n_kv == _cdiv(n, KEY_BLOCK)
     assert p.num_tiles == b * h * p.n_pairs
     assert p.grid == min(p.num_tiles, sms)
@@ -86,7 +86,7 @@ def test_units_cover_every_slice_pair_once(sched, b, h, n, causal):
 @pytest.mark.parametrize("causal", [False, True])
 def test_order_groups_slices_and_puts_heavy_causal_units_first(sched, causal):
     b, h, n, sms = 8, 32, 4096, 148
-    p = sched.s_plan(b, h, n, 128, KEY_BLOCK, sms)
+    p = sched.s_plan(b, h, n, 128, KEY_BLOCK, sms, int(causal))
     units = [sched.s_decode(t, b, h, n, p.n_pairs, p.n_kv, p.group_bh, KEY_BLOCK, int(causal))
              for t in range(p.num_tiles)]
     per_group = p.group_bh * p.n_pairs
@@ -101,11 +101,11 @@ def test_order_groups_slices_and_puts_heavy_causal_units_first(sched, causal):
             assert len(set(work)) == 1
 
 
-def test_groups_fit_the_l2_budget_and_are_balanced(sched):
+def test_causal_groups_fit_the_l2_budget_and_are_balanced(sched):
     budget = 64 << 20  # kL2GroupBytes
     for b, h, n, d in [(8, 32, 4096, 128), (2, 32, 16384, 128), (16, 16, 2048, 32), (1, 32, 4096, 128),
                        (1, 8, 16384, 128), (3, 7, 1000, 64), (1, 200, 129, 128)]:
-        p = sched.s_plan(b, h, n, d, KEY_BLOCK, 148)
+        p = sched.s_plan(b, h, n, d, KEY_BLOCK, 148, 1)
         bh = b * h
         kv = 4 * n * d  # K and V bytes of one slice
         wave = _cdiv(148, p.n_pairs)
@@ -117,13 +117,20 @@ def test_groups_fit_the_l2_budget_and_are_balanced(sched):
         assert groups * p.group_bh >= bh
     # the headline configuration: 8 groups of 32 slices (64 MB of K and V each);
     # a rank of an 8-way split of it (32 slices) is one group
-    assert sched.s_plan(8, 32, 4096, 128, KEY_BLOCK, 148).group_bh == 32
-    assert sched.s_plan(1, 32, 4096, 128, KEY_BLOCK, 148).group_bh == 32
-    # short sequences: at least one wave of units per group
-    p = sched.s_plan(4, 16, 1024, 64, KEY_BLOCK, 148)
-    assert p.group_bh == 64
-    p = sched.s_plan(1, 1, 4096, 128, KEY_BLOCK, 148)
+    assert sched.s_plan(8, 32, 4096, 128, KEY_BLOCK, 148, 1).group_bh == 32
+    assert sched.s_plan(1, 32, 4096, 128, KEY_BLOCK, 148, 1).group_bh == 32
+    p = sched.s_plan(1, 1, 4096, 128, KEY_BLOCK, 148, 1)
     assert p.group_bh == 1 and p.grid == 16
+
+
+def test_non_causal_groups_are_one_wave(sched):
+    # equal-cost units: a group is about one unit per SM
+    p = sched.s_plan(16, 16, 2048, 128, KEY_BLOCK, 148, 0)
+    assert p.n_pairs == 8 and p.group_bh == 19
+    p = sched.s_plan(4, 16, 1024, 64, KEY_BLOCK, 148, 0)
+    assert p.group_bh == 37
+    p = sched.s_plan(8, 32, 4096, 128, KEY_BLOCK, 148, 0)
+    assert p.group_bh == 10
 
 
 def _makespan(units, sms, cost):
@@ -148,7 +155,7 @@ def test_causal_headline_share_is_balanced(sched, ranks):
     percent more work than the average, in a model where a key block costs 2
     with both query tiles busy, 1.6 with one, and every unit 1 more."""
     b, h, n, sms = 1, 256 // ranks, 4096, 148
-    p = sched.s_plan(b, h, n, 128, KEY_BLOCK, sms)
+    p = sched.s_plan(b, h, n, 128, KEY_BLOCK, sms, 1)
     units = [sched.s_decode(t, b, h, n, p.n_pairs, p.n_kv, p.group_bh, KEY_BLOCK, 1) for t in range(p.num_tiles)]
 
     def cost(u):
