@@ -77,3 +77,23 @@ def test_benchmark_loop_and_interface_calls():
         fa2.forward(q.float(), k.float(), v.float())
     with pytest.raises(RuntimeError, match="head_dim"):
         fa2.forward(q[..., :48], k[..., :48], v[..., :48])
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("causal", [False, True])
+def test_vs_library_attention(dtype, causal):
+    """benchmark/python/tests/test_pybind_vs_official_correctness.py:95-160 compares
+    fa2.forward with an official library kernel on its default cases (2x4x{128,256,
+    512}x128, inputs from generate_qkv) at fp16 2e-2 / bf16 3e-2 (atol = rtol).
+    Here the library kernel is PyTorch's scaled_dot_product_attention on the same
+    device; the causal variant uses its is_causal mask (col > row masked)."""
+    import torch.nn.functional as F
+
+    tol = 2e-2 if dtype == torch.float16 else 3e-2
+    for i, (b, h, n, d) in enumerate([(2, 4, 128, 128), (2, 4, 256, 128), (2, 4, 512, 128)]):
+        q, k, v, _ = generate_qkv(batch_size=b, n_heads=h, seq_len=n, d_head=d, dtype=dtype, device="cuda",
+                                  input_mode="random", seed=1234, case_index=i)
+        out = fa2.forward(q, k, v, causal=causal)
+        official = F.scaled_dot_product_attention(q, k, v, is_causal=causal)
+        diff = (official.float() - out.float()).abs()
+        assert torch.allclose(official.float(), out.float(), atol=tol, rtol=tol), (i, float(diff.max()))
