@@ -123,3 +123,32 @@ def test_verify_accepts_the_exact_result_and_rejects_a_planted_error():
     assert not r["ok"]
     r = bench.verify(cfg, (q, k, v), o_all, l_all + 1e-3, [0, 2], torch.device("cpu"))
     assert not r["ok"]
+
+
+def test_rank_inputs_partition_the_configuration():
+    """Strong scaling: rank r's Q, K, V are slices [r*S/N, (r+1)*S/N) of the one
+    seeded configuration, and the ranks together hold every slice once."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    from flash_attention_runtime.inputs import CONFIGS, generate
+
+    cfg = CONFIGS["cfg0"]  # 4 slices
+    q, k, v = generate(cfg)
+    flat = q.reshape(cfg.slices, cfg.seq_len, cfg.head_dim)
+    got = []
+    for r in range(3):
+        (qr, kr, vr), full, first = bench.rank_inputs(cfg, r, 3, "strong")
+        assert qr.shape[0] == 1 and qr.is_contiguous()
+        assert torch.equal(full[0], q)
+        n = qr.shape[1]
+        assert torch.equal(qr[0], flat[first:first + n])
+        got.append((first, n))
+    assert got == [(0, 2), (2, 1), (3, 1)]
+    # weak scaling: every rank a full batch of its own seed
+    (q0, _, _), _, _ = bench.rank_inputs(cfg, 0, 2, "weak")
+    (q1, _, _), _, _ = bench.rank_inputs(cfg, 1, 2, "weak")
+    assert q0.shape == q.shape and torch.equal(q0, q) and not torch.equal(q1, q)
+    # --share-of 8 on one process stands in for rank 0 of an 8-way split
+    assert bench.parse_args(["--share-of", "8"]).share_of == 8
+    assert bench.input_copies(CONFIGS["cfg2"], 8, "strong") == 3
