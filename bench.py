@@ -53,7 +53,7 @@ METRIC = ("attention fwd TFLOPS of the whole job over n_gpus (4*B*H*N^2*d/t, hal
           "per_gpu = value/n_gpus, and % of dense bf16 peak in roofline")
 REF_BUDGET_S = 150.0
 E2E_BUDGET_S = 10.0   # the end-to-end leg runs min(--steps, what fits in this) steps
-E2E_CHUNKS = 32           # at most; a chunk carries at least E2E_CHUNK_BYTES of Q+K+V
+E2E_CHUNKS = 8            # at most; a chunk carries at least E2E_CHUNK_BYTES of Q+K+V
 E2E_CHUNK_BYTES = 16 << 20
 SUSTAINED_AFTER_S = 1.0  # timed regions at least this long are compared with the sustained peak
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
@@ -534,9 +534,10 @@ def run_ours(args, cfg: AttnConfig):
     # ---- end to end through the public API: pinned host -> device, forward, device -> host.
     # The rank's slices go through in chunks so the upload of chunk c+1 (one copy
     # engine), the forward of chunk c and the download of chunk c-1 (the other copy
-    # engine) overlap; only the last chunk's forward and download follow the uploads,
-    # so chunks are small (up to E2E_CHUNKS, at least E2E_CHUNK_BYTES of Q+K+V
-    # each).  Events keep buffer reuse across steps ordered.
+    # engine) overlap; only the last chunk's forward and download follow the uploads.
+    # Up to E2E_CHUNKS chunks of at least E2E_CHUNK_BYTES of Q+K+V: 32 chunks measured
+    # slower than 8 (five copies per chunk, each with its own set-up cost).  Events
+    # keep buffer reuse across steps ordered.
     s_all = n_slices
     flat = lambda t: t.reshape(1, s_all, *t.shape[2:])  # noqa: E731
     qp, kp, vp = (flat(t).pin_memory() for t in (qh, kh, vh))
