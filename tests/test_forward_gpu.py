@@ -256,3 +256,32 @@ def test_cfg3_strided_slices_and_properties():
     l0 = (qd[:, :, 0].float() * kd[:, :, 0].float()).sum(-1) * cfg.scale
     assert float((lse[:, :, 0] - l0).abs().max()) < 1e-4 * max(1.0, float(l0.abs().max()))
     assert bool(torch.isfinite(lse).all())
+
+
+@pytest.mark.parametrize("shape,dtype,causal", [
+    ((1, 8, 3001, 128), torch.bfloat16, True),    # ragged causal, 12 units per slice, last one partial
+    ((2, 3, 2049, 64), torch.float16, False),     # one row past a 2048-row multiple
+    ((1, 4, 5000, 32), torch.float16, True),      # long ragged causal at the smallest head dim
+])
+def test_large_ragged_sequences(shape, dtype, causal):
+    """Sequence lengths far from the 128-row tiles at sizes with many key blocks per
+    unit: every slice against the oracle."""
+    q, k, v = make_random(shape, dtype, seed=61 + shape[2])
+    _run_and_check(q, k, v, causal)
+
+
+def test_thousands_of_tiny_slices():
+    """B64 H64 N64 d32: 4096 slices of one work unit each, so every CTA chains about
+    28 units across several scheduling groups; every slice against the oracle."""
+    q, k, v = make_random((64, 64, 64, 32), torch.bfloat16, seed=62)
+    _run_and_check(q, k, v, causal=True)
+
+
+@pytest.mark.parametrize("scale", [1e-3, 2.0])
+def test_extreme_softmax_scales(scale):
+    """A scale of 1e-3 makes the attention nearly uniform over the keys (a long
+    accumulation of similar P); 2.0 makes it nearly one-hot (rescales of O as the
+    running maximum jumps)."""
+    q, k, v = make_random((2, 3, 777, 64), torch.float16, seed=63)
+    _run_and_check(q, k, v, causal=False, scale=scale)
+    _run_and_check(q, k, v, causal=True, scale=scale)
