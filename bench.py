@@ -142,6 +142,13 @@ class ClockSampler:
         self.thread = threading.Thread(target=self._read, daemon=True)
         self.thread.start()
 
+    def wait_first_sample(self, timeout_s: float = 10.0):
+        """Block until nvidia-smi has reported once (its NVML start-up is over), so
+        that start-up does not overlap the timed region."""
+        t_end = time.time() + timeout_s
+        while self.proc is not None and not self.samples and time.time() < t_end and self.proc.poll() is None:
+            time.sleep(0.01)
+
     def _read(self):
         for line in self.proc.stdout:
             parts = [x.strip() for x in line.split(",")]
@@ -446,6 +453,11 @@ def run_ours(args, cfg: AttnConfig):
     # --share-of N on a single process stands in for rank 0 of an N-way strong split
     share = args.share_of if (world == 1 and args.scaling == "strong" and args.share_of > 1) else 1
     split_world = world * share
+    # nvidia-smi starts now and reports once before the device work begins: its
+    # start-up on every rank at once, inside a timed region of a few milliseconds
+    # (20 steps of one rank's share), would otherwise be timed with it.
+    sampler = ClockSampler(local)
+    sampler.start()
     (qh, kh, vh), full, first_slice = rank_inputs(cfg, rank, split_world, args.scaling)
     n_slices = qh.shape[0] * qh.shape[1]
     n_copies = input_copies(cfg, split_world, args.scaling)
@@ -461,8 +473,7 @@ def run_ours(args, cfg: AttnConfig):
         fa.ext_forward(cq, ck, cv, co, False, cfg.scale, cfg.causal, cl)
 
     fa.reset_device_status(dev)
-    sampler = ClockSampler(local)
-    sampler.start()
+    sampler.wait_first_sample()
     warmup = max(args.warmup, 3)
     for i in range(warmup):
         step(i)
