@@ -104,8 +104,8 @@ FA_API int fa_fwd_sm100(const fa_fwd_params* params, void* stream);
  * cudaMemsetAsync before every launch; a scheduler needing more than 256 bytes
  * is rejected with FA_ERR_BAD_SHAPE.  No cudaMalloc / cudaFree is called.  The
  * first call on a device looks up the array's address (cudaGetSymbolAddress)
- * with that device current, and must therefore come before any stream capture;
- * after a cudaDeviceReset of that device the cached address is stale.  All calls
+ * with that device current and caches it; after a cudaDeviceReset of that
+ * device the cached address is stale.  All calls
  * on a device share the array: calls whose kernels overlap on the GPU race on it. */
 FA_API int fa_fwd_sm100_noalloc(const fa_fwd_params* params, void* stream);
 
