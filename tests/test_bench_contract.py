@@ -44,6 +44,27 @@ def test_reference_arm_prints_one_contract_line():
     assert "rotating" in d["config"]["l2"]
 
 
+def test_reference_arm_under_torchrun_prints_once_from_rank_0():
+    """Launched like the multi-GPU arms (torchrun, two ranks): rank 0 alone runs the
+    CPU reference and prints its line; the other rank exits 0 without output."""
+    import os
+    import socket
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    env = {**os.environ, "OMP_NUM_THREADS": "1"}
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                        "--master-addr", "127.0.0.1", "--master-port", str(port), str(ROOT / "bench.py"),
+                        "--impl", "reference", "--gpus", "2", "--workload", "cfg0", "--steps", "1", "--warmup", "1"],
+                       capture_output=True, text=True, timeout=600, cwd=ROOT, env=env)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.strip().splitlines() if ln.startswith("{")]
+    assert len(lines) == 1, r.stdout
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["value"] > 0 and d["config"]["workload"] == "cfg0"
+
+
 def test_our_arm_fails_loudly_without_a_gpu():
     if torch.cuda.is_available():
         pytest.skip("a GPU is present")
