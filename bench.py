@@ -55,6 +55,7 @@ REF_BUDGET_S = 150.0
 E2E_BUDGET_S = 10.0   # the end-to-end leg runs min(--steps, what fits in this) steps
 E2E_CHUNKS = 8            # at most; a chunk carries at least E2E_CHUNK_BYTES of Q+K+V
 E2E_CHUNK_BYTES = 16 << 20
+PRE_SPIN_CYCLES = 2_000_000  # GPU cycles the stream spins before the timed region (about 1 ms at 1965 MHz)
 SUSTAINED_AFTER_S = 1.0  # timed regions at least this long are compared with the sustained peak
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 ATOL = {torch.float16: 2e-3, torch.bfloat16: 1e-2}
@@ -482,6 +483,12 @@ def run_ours(args, cfg: AttnConfig):
     torch.cuda.synchronize(dev)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t_wall0 = time.time()
+    # The stream first spins for about a millisecond, so that the host enqueues
+    # the start event and the first launches while the GPU is busy: the timed
+    # region then holds the K launches back to back, without the host's latency
+    # to submit the first one (tens of microseconds through Python, against a
+    # region of a few milliseconds for one rank's share).  Host costs are in e2e.
+    torch.cuda._sleep(PRE_SPIN_CYCLES)
     start.record(stream)
     for i in range(args.steps):
         step(i)
